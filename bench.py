@@ -1,0 +1,457 @@
+"""Benchmark: 7B-shape batched greedy decode on B200 (sm_100a kernels).
+
+Workload (the decode config): Llama-2-7B shape (32 layers, hidden 4096,
+32 heads x 128, FFN 11008, vocab 32000), random-init bf16 weights ~N(0, 0.02)
+with RMSNorm weights 1.0, 256 prompts of 512 tokens drawn uniformly over the
+vocabulary (seed 3), greedy decode.  The 256 sequences are split in
+contiguous chunks over the ranks (256/128/64/32 per GPU at 1/2/4/8 GPUs), one
+process per GPU, full weight replica each, no collective on the data path.
+
+A "step" is one batched decode step of the whole model for the rank's
+sequences (embedding -> 32 layers -> norm -> lm_head -> argmax), replayed from
+one CUDA graph.  Untimed steps run first so that the timed steps are centred
+on the mean context of a 128-token generation (prompt + 64).  Every step
+reads ~90 GB (weights + KV cache) at N=1, far more than L2: no flush needed.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  ``--impl reference`` times the CPU oracle port
+of the reference's PyTorch path on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "7B-shape decode tok/s at 1/2/4/8 B200; per-kernel % of HBM / TC roofline"
+UNIT = "tok/s"
+GLOBAL_BATCH = 256
+PROMPT_LEN = 512
+NEW_TOKENS = 128
+SEED = 3
+# ncu dram bytes (read + write) per decode-attention launch, layer cache of the
+# 256 x ~576-token state; see profiles/decode_attention_7b.md (null until captured)
+DECODE_ATTN_NCU_TRAFFIC = None
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=GLOBAL_BATCH)
+    ap.add_argument("--prompt-len", type=int, default=PROMPT_LEN)
+    ap.add_argument("--layers", type=int, default=32, help="(debug only) fewer layers")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = tempfile.mktemp(prefix="clocks_", suffix=".csv")
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        under = [s for s in sm if s > 0.5 * (max(smax) if smax else 1)] or sm
+        return {"sm_mhz": statistics.median(under) if under else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def shard(global_batch: int, world: int, rank: int):
+    """Contiguous chunk of sequences for this rank (256/N each)."""
+    per = global_batch // world
+    extra = global_batch % world
+    start = rank * per + min(rank, extra)
+    return start, per + (1 if rank < extra else 0)
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.zeros(1, device="cuda")
+        dist.all_reduce(t)
+    torch.cuda.synchronize()
+
+
+def model_config(layers: int, max_seq: int):
+    from llama_pure_compute_b200.config import PRESETS, LlamaModelConfig
+    base = PRESETS["llama-2-7b"]
+    return LlamaModelConfig(vocab_size=base.vocab_size, dim=base.dim, inter_dim=base.inter_dim,
+                            num_layers=layers, num_heads=base.num_heads,
+                            num_kv_heads=base.num_kv_heads, max_seq_len=max_seq,
+                            rms_norm_eps=1e-5, rope_theta=10000.0)
+
+
+def prompts_for(rank_start: int, count: int, prompt_len: int, global_batch: int):
+    g = torch.Generator().manual_seed(SEED)
+    allp = torch.randint(0, 32000, (global_batch, prompt_len), generator=g)
+    return allp[rank_start:rank_start + count]
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle port of the reference's PyTorch CPU path
+# ---------------------------------------------------------------------------
+def cpu_decode_baseline(layers: int, seconds: float, batch: int = 4, ctx: int = 576):
+    """Times decode steps of the 7B shape on the host cores with the CPU oracle
+    (fp32 torch on CPU).  Bounded sample: `batch` sequences with a random
+    `ctx`-token KV cache, as many steps as fit in ~`seconds`; the 32 layers
+    share one layer's random weights (same arithmetic and per-layer weight
+    bytes; keeps host memory and set-up time small)."""
+    from oracle.model_ref import OracleLlama
+    torch.manual_seed(SEED)
+    cfg = dict(vocab_size=32000, dim=4096, inter_dim=11008, num_layers=layers, num_heads=32,
+               num_kv_heads=32, rms_norm_eps=1e-5, rope_theta=10000.0)
+    D, I, V = 4096, 11008, 32000
+    layer = {
+        "input_layernorm.weight": torch.ones(D),
+        "self_attn.q_proj.weight": torch.randn(D, D) * 0.02,
+        "self_attn.k_proj.weight": torch.randn(D, D) * 0.02,
+        "self_attn.v_proj.weight": torch.randn(D, D) * 0.02,
+        "self_attn.o_proj.weight": torch.randn(D, D) * 0.02,
+        "post_attention_layernorm.weight": torch.ones(D),
+        "gate_proj.weight": torch.randn(I, D) * 0.02,
+        "up_proj.weight": torch.randn(I, D) * 0.02,
+        "down_proj.weight": torch.randn(D, I) * 0.02,
+    }
+    sd = {"model.embed_tokens.weight": torch.randn(V, D) * 0.02, "model.norm.weight": torch.ones(D),
+          "lm_head.weight": torch.randn(V, D) * 0.02}
+    for i in range(layers):
+        for k, v in layer.items():
+            sd[f"model.layers.{i}.{k}"] = v
+    orc = OracleLlama(cfg, sd, max_seq_len=ctx + 256)
+    cache = [[torch.randn(batch, 32, ctx, 128), torch.randn(batch, 32, ctx, 128)]
+             for _ in range(layers)]
+    tok = torch.randint(0, V, (batch, 1))
+    times = []
+    t_end = time.perf_counter() + seconds
+    pos = ctx
+    with torch.no_grad():
+        while True:
+            t0 = time.perf_counter()
+            logits = orc.forward(tok, torch.full((batch, 1), pos), cache)
+            tok = logits[:, -1].argmax(-1, keepdim=True)
+            times.append(time.perf_counter() - t0)
+            pos += 1
+            if time.perf_counter() > t_end and len(times) >= 2:
+                break
+    steady = times[1:] if len(times) > 1 else times
+    sec = statistics.median(steady)
+    return {"value": batch / sec, "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": (f"CPU oracle (fp32 torch on host, {torch.get_num_threads()} threads): "
+                       f"{len(times)} decode steps of {batch} sequences at context {ctx}..{pos - 1}, "
+                       f"{layers} layers sharing one layer's random weights; median step "
+                       f"{sec * 1e3:.1f} ms")}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    cb = cpu_decode_baseline(args.layers, args.cpu_seconds * max(1, args.steps) / 20.0)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(cb["value"], 3), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(4 / cb["value"] * 1e3, 2), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "llama-2-7b batched greedy decode (bounded CPU sample)",
+                   "global_batch": GLOBAL_BATCH, "prompt_len": args.prompt_len,
+                   "new_tokens": NEW_TOKENS},
+        "cpu_baseline": cb,
+        "e2e": {"value": round(cb["value"], 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU run
+# ---------------------------------------------------------------------------
+def run_ours(args, world, rank, local):
+    from llama_pure_compute_b200 import _lib
+    from llama_pure_compute_b200.generate import BatchedGreedyDecoder
+    from llama_pure_compute_b200.kv_manager import KVCacheManager
+    from llama_pure_compute_b200.model import LlamaForCausalLM
+    from llama_pure_compute_b200.ops import decode_attention
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    _lib.load()
+    start, count = shard(args.batch, world, rank)
+    mean_ctx = args.prompt_len + NEW_TOKENS // 2
+    pre_steps = max(args.warmup, mean_ctx - args.prompt_len - args.steps // 2)
+    max_seq = args.prompt_len + max(NEW_TOKENS, pre_steps + args.steps + 2)
+    cfg = model_config(args.layers, max_seq)
+
+    model = LlamaForCausalLM.random_init(cfg, device=dev, dtype=torch.bfloat16, seed=SEED)
+    kv = KVCacheManager(num_layers=cfg.num_layers, max_batch_size=count, max_seq_len=max_seq,
+                        n_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim, dtype=torch.bfloat16,
+                        device=dev)
+    prompts = prompts_for(start, count, args.prompt_len, args.batch)
+    dec = BatchedGreedyDecoder(model, kv, count, use_cuda_graph=True)
+
+    barrier(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    dec.prefill(prompts)
+    t1.record()
+    torch.cuda.synchronize()
+    prefill_ms = max_over_ranks(t0.elapsed_time(t1), world)
+
+    n0 = _lib.launch_count
+    dec.capture()
+    launches_per_step = _lib.launch_count - n0
+
+    clocks = ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                          int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local]))
+    clocks.start()
+    for _ in range(pre_steps):  # untimed warm-up steps (also move to the mean context)
+        dec.step()
+    barrier(world)
+    ctx_first = int(dec.positions[0, 0].item())
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        dec.step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = e0.elapsed_time(e1)
+    ms_max = max_over_ranks(ms, world)
+    tok_s = args.batch * args.steps / (ms_max / 1e3)
+
+    # ---- e2e: public API, host token buffers, H2D + D2H inside every step ----
+    B = count
+    host_tok = torch.empty(B, dtype=torch.long, pin_memory=True)
+    host_pos = torch.empty(B, dtype=torch.long, pin_memory=True)
+    host_out = torch.empty(B, dtype=torch.long, pin_memory=True)
+    host_tok.copy_(dec.tokens[:, 0].cpu())
+    host_pos.copy_(dec.positions[:, 0].cpu())
+    e_steps = max(2, min(args.steps, 20))
+    barrier(world)
+    w0 = time.perf_counter()
+    s0 = torch.cuda.Event(enable_timing=True)
+    s1 = torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(e_steps):
+        dec.tokens[:, 0].copy_(host_tok, non_blocking=True)
+        dec.positions[:, 0].copy_(host_pos, non_blocking=True)
+        out = dec.step()
+        host_out.copy_(out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        host_tok.copy_(host_out)
+        host_pos.add_(1)
+    s1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(s0.elapsed_time(s1), world)
+    wall_e2e = max_over_ranks((time.perf_counter() - w0) * 1e3, world)
+    e2e_tok_s = args.batch * e_steps / (e2e_ms / 1e3)
+    clk = clocks.stop()
+
+    # ---- dominant kernel: split-KV decode attention, timed standalone on the
+    # final decode state (layer 0 cache, current per-sequence lengths) ----
+    lens = kv.seq_lens[:B].clone()
+    q = torch.randn(B, cfg.num_heads, cfg.head_dim, device=dev, dtype=torch.bfloat16)
+    ws = model.model._workspace(B, kv.max_seq_len, dev)
+    outb = torch.empty_like(q)
+    for _ in range(3):
+        decode_attention(q, kv.k_cache[0], kv.v_cache[0], lens, None, outb, ws)
+    a0 = torch.cuda.Event(enable_timing=True)
+    a1 = torch.cuda.Event(enable_timing=True)
+    reps = 10
+    a0.record()
+    for i in range(reps):
+        decode_attention(q, kv.k_cache[i % cfg.num_layers], kv.v_cache[i % cfg.num_layers], lens,
+                         None, outb, ws)
+    a1.record()
+    torch.cuda.synchronize()
+    attn_us = a0.elapsed_time(a1) * 1e3 / reps
+    ctx_sum = int(lens.sum().item())
+    attn_bytes = ctx_sum * cfg.num_kv_heads * cfg.head_dim * 2 * 2 + 2 * B * cfg.num_heads * cfg.head_dim * 2
+    attn_gbs = attn_bytes / (attn_us * 1e-6) / 1e9
+    peaks = {}
+    try:
+        peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    # algorithmic bytes of one decode step: every weight once (the embedding
+    # table only for the B gathered rows) + the KV cache at the timed steps'
+    # mean context
+    emb = model.model.embed_tokens.weight
+    weight_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
+    weight_bytes += (B - emb.shape[0]) * emb.shape[1] * emb.element_size()
+    mean_ctx_timed = ctx_first + (args.steps + 1) / 2
+    kv_bytes = int(B * mean_ctx_timed) * cfg.num_layers * 2 * cfg.num_kv_heads * cfg.head_dim * 2
+    step_bytes = weight_bytes + kv_bytes
+    dec.release()
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            torch.set_num_threads(os.cpu_count() or 1)
+            cpu = cpu_decode_baseline(args.layers, args.cpu_seconds)
+        line = {
+            "metric": METRIC,
+            "value": round(tok_s, 1),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": pre_steps,
+            "ms_per_step": round(ms_max / args.steps, 3),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (random-init weights, uniform random prompt ids)",
+            "config": {
+                "workload": "llama-2-7b batched greedy decode, 256 prompts x 512 tokens, "
+                            "steps timed around mean context 576",
+                "model": "llama-2-7b shape (32L, 4096, 32x128 heads, FFN 11008, vocab 32000)",
+                "global_batch": args.batch,
+                "per_gpu_batch": count,
+                "seq_len": args.prompt_len,
+                "context_timed": [ctx_first, ctx_first + args.steps - 1],
+                "parallelism": f"sequence-sharded replicas x{world} (no collective)",
+                "l2": "inputs larger than L2 (each step streams ~13 GB weights + KV cache)",
+                "layers": cfg.num_layers,
+            },
+            "clocks": clk,
+            "e2e": {"value": round(e2e_tok_s, 1), "unit": UNIT, "h2d_bytes_per_step": 2 * 8 * B,
+                    "d2h_bytes_per_step": 8 * B, "steps": e_steps,
+                    "wall_ms": round(wall_e2e, 2)},
+            "gpu_launches": launches_per_step * args.steps,
+            "roofline": {
+                "kernel": "decode_split_kernel + decode_combine_kernel (split-KV decode attention)",
+                "bound": "hbm",
+                "achieved": round(attn_gbs, 1),
+                "peak": hbm_peak,
+                "unit": "GB/s",
+                "frac": round(attn_gbs / hbm_peak, 4),
+                "traffic": DECODE_ATTN_NCU_TRAFFIC,
+                "algorithmic_bytes_per_launch": attn_bytes,
+                "launch_us": round(attn_us, 2),
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs (burst)" if peaks else "fallback 6650",
+            },
+            "step_roofline": {
+                "bytes_per_step": step_bytes,
+                "achieved_gbs": round(step_bytes / (ms_max / args.steps * 1e-3) / 1e9, 1),
+                "frac": round(step_bytes / (ms_max / args.steps * 1e-3) / 1e9 / hbm_peak, 4),
+            },
+            "prefill": {"tokens": args.batch * args.prompt_len,
+                        "ms": round(prefill_ms, 1),
+                        "tok_s": round(args.batch * args.prompt_len / (prefill_ms / 1e3), 1)},
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup() if torch.cuda.is_available() else (1, 0, 0)
+    if args.impl == "reference":
+        try:
+            run_reference(args, world, rank)
+        finally:
+            if world > 1:
+                import torch.distributed as dist
+                dist.destroy_process_group()
+        return
+    if not torch.cuda.is_available():
+        print(json.dumps({"metric": METRIC, "error": "no CUDA device"}))
+        sys.exit(1)
+    try:
+        run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

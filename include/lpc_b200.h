@@ -1,0 +1,182 @@
+/*
+ * lpc_b200.h -- C ABI of the B200 (sm_100a) Llama inference hot path.
+ *
+ * Plain pointers, sizes and a CUDA stream handle (passed as void*); no torch
+ * or C++ types.  Every entry point:
+ *   - validates its arguments on the host and returns LPC_ERR_INVALID (the
+ *     Python layer raises ValueError) or LPC_ERR_UNSUPPORTED (TypeError)
+ *     with a message available from lpc_last_error();
+ *   - enqueues its kernels on `stream` and returns without synchronising;
+ *   - returns LPC_ERR_CUDA if a launch fails (RuntimeError).
+ * Device pointers must be 16-byte aligned and tensors contiguous unless a
+ * stride argument says otherwise.  Nothing here allocates device memory:
+ * ops that need scratch take a caller-provided workspace whose size comes
+ * from the matching *_workspace_bytes() query.
+ *
+ * Reference citations are paths inside the Llama_Pure_Compute project.
+ */
+#ifndef LPC_B200_H
+#define LPC_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LPC_API __attribute__((visibility("default")))
+#else
+#define LPC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LPC_OK 0
+#define LPC_ERR_INVALID 1      /* bad shape / pointer / argument (ValueError)  */
+#define LPC_ERR_UNSUPPORTED 2  /* dtype or size the kernels do not cover (TypeError) */
+#define LPC_ERR_CUDA 3         /* a CUDA call or launch failed (RuntimeError)  */
+
+#define LPC_DTYPE_F32 0
+#define LPC_DTYPE_F16 1
+#define LPC_DTYPE_BF16 2
+
+/* Library version, e.g. 100 for 0.1.0. */
+LPC_API int lpc_version(void);
+
+/* Message describing the last non-zero status returned on this host thread. */
+LPC_API const char* lpc_last_error(void);
+
+/* OR of the device status words of all kernels (timeouts of bounded waits,
+ * failed device-side bounds checks) since the last call; clears them.
+ * Synchronises the current device.  Returns -1 if the read itself failed. */
+LPC_API int lpc_device_status(void);
+
+/*
+ * In-place KV-cache append.
+ * Replaces: `_backend.update_kv_cache` (src/llama_pure_compute/ops.py:139-166,
+ *           src/csrc/ops/kv_cache.cu:13-43 and :152-198).
+ * key_src/value_src: [num_tokens, num_kv_heads, head_dim], row stride
+ *   `src_token_stride` elements between tokens (num_kv_heads*head_dim when packed).
+ * key_cache/value_cache: [max_batch, num_kv_heads, max_seq_len, head_dim].
+ * slot_mapping: int64 [num_tokens] or NULL (slot = token index).
+ *   (b, pos) = divmod(slot, max_seq_len); slot < 0 is skipped; a slot at or
+ *   beyond max_batch*max_seq_len is skipped and flagged in lpc_device_status().
+ * elem_bytes: 2 or 4 (the op is a copy, bit-exact for every dtype).
+ */
+LPC_API int lpc_update_kv_cache(const void* key_src, const void* value_src, void* key_cache,
+                        void* value_cache, const int64_t* slot_mapping, int64_t num_tokens,
+                        int64_t src_token_stride, int num_kv_heads, int head_dim,
+                        int64_t max_batch, int64_t max_seq_len, int elem_bytes, void* stream);
+
+/*
+ * In-place rotary embedding (half-split / "rotate_half" convention).
+ * Replaces: `_backend.rope_forward` (src/llama_pure_compute/ops.py:95-117,
+ *           src/csrc/ops/rope.cu:10-84 and :143-193); semantics of
+ *           `_rope_forward_pytorch` (ops.py:27-42).
+ * q: [num_tokens, num_heads, head_dim], k: [num_tokens, num_kv_heads, head_dim].
+ * Table modes:
+ *   table_mode 0: cos/sin are [table_rows, head_dim/2]; row = position_ids[t]
+ *                 (or t when position_ids is NULL)  -- rope.cu convention.
+ *   table_mode 1: cos/sin are [num_tokens, head_dim]; row = t (tables already
+ *                 gathered per token, as LlamaModel.forward passes them,
+ *                 src/llama_pure_compute/model.py:388-393).
+ * out[d]     = q[d]*cos[d]     - q[d+h]*sin[d]
+ * out[d+h]   = q[d+h]*cos[d+h] + q[d]*sin[d+h]   (h = head_dim/2; mode 0 uses
+ *                                                 column d for both halves)
+ * computed in fp32 with single-rounded products and sum, rounded once to the
+ * output dtype.  q_dtype is shared by q and k; table_dtype by cos and sin.
+ */
+LPC_API int lpc_rope_forward(void* q, void* k, const void* cos, const void* sin,
+                     const int64_t* position_ids, int64_t num_tokens, int num_heads,
+                     int num_kv_heads, int head_dim, int table_mode, int64_t table_rows,
+                     int q_dtype, int table_dtype, void* stream);
+
+/*
+ * Fused decode/prefill attention prologue: RoPE on q and k taken straight from
+ * the fused QKV projection, q written head-major for attention, rotated k and
+ * v appended into the caches.
+ * Replaces the sequence rope_forward -> transpose(1,2).contiguous() x3 ->
+ *   KVCacheManager.update (src/llama_pure_compute/model.py:146-168,
+ *   src/llama_pure_compute/kv_manager.py:207-317).
+ * qkv: [batch, seq, (num_heads + 2*num_kv_heads) * head_dim] (q | k | v).
+ * positions: int64 [batch, seq] absolute positions; row b of the caches is
+ *   written at pos = positions[b, s]; a negative position skips the token.
+ * cos/sin: [table_rows, head_dim] full-width tables (precompute_freqs_cis,
+ *   model.py:28-64) in table_dtype.
+ * q_out: [batch, num_heads, seq, head_dim].
+ */
+LPC_API int lpc_rope_kv_append(const void* qkv, const int64_t* positions, const void* cos,
+                       const void* sin, int64_t table_rows, void* q_out, void* key_cache,
+                       void* value_cache, int64_t batch, int64_t seq, int num_heads,
+                       int num_kv_heads, int head_dim, int64_t max_batch, int64_t max_seq_len,
+                       int dtype, int table_dtype, void* stream);
+
+/*
+ * RMSNorm: y = x * rsqrt(mean(x^2) + eps) * w, fp32 math, output in x's dtype.
+ * Replaces: `rmsnorm_triton_forward` / `_rmsnorm_pytorch_fallback`
+ *           (src/llama_pure_compute/triton_kernels/rmsnorm.py:20-96).
+ * x, y: [rows, dim]; w: [dim] in w_dtype.
+ */
+LPC_API int lpc_rmsnorm_forward(const void* x, const void* w, void* y, int64_t rows, int dim, float eps,
+                        int dtype, int w_dtype, void* stream);
+
+/*
+ * Fused RMSNorm + SwiGLU: out = silu(norm(x) W_gate^T) * (norm(x) W_up^T).
+ * Replaces: `_backend.rmsswiglu_forward` (src/llama_pure_compute/ops.py:120-136,
+ *           src/csrc/ops/rmsswiglu.cu:151-282); semantics of
+ *           `_rmsswiglu_forward_pytorch` (ops.py:45-59).
+ * x: [tokens, dim]; rms_weight: [dim] (w_dtype); out: [tokens, inter].
+ * gate_w, up_w: [inter, dim].  up_w == NULL means gate_w is the fused
+ *   [2*inter, dim] matrix (gate rows first), as rmsswiglu.cu:167-173 accepts.
+ * bf16 / fp16: tcgen05 tensor-core GEMM with the SiLU*up epilogue; needs
+ *   lpc_rmsswiglu_workspace_bytes() of workspace (the normalised activations).
+ * fp32: CUDA-core streaming kernel (no TF32), workspace unused.
+ * eps must be > 0.
+ */
+LPC_API int64_t lpc_rmsswiglu_workspace_bytes(int64_t tokens, int dim, int dtype);
+LPC_API int lpc_rmsswiglu_forward(const void* x, const void* rms_weight, const void* gate_w,
+                          const void* up_w, void* out, void* workspace, int64_t workspace_bytes,
+                          int64_t tokens, int dim, int inter, float eps, int dtype, int w_dtype,
+                          void* stream);
+
+/*
+ * Causal / non-causal flash attention with q_len <= kv_len, queries aligned to
+ * the END of the key sequence (bottom-right causal mask), fp32 accumulation.
+ * Replaces: `flash_attention_v2` prefill path
+ *           (src/llama_pure_compute/triton_kernels/flash_attention.py:88-432,
+ *           :998-1155); mask semantics of tests/test_attention_correctness.py:10-76.
+ * q: [batch, heads, q_len, head_dim]; k, v: [batch, kv_heads, kv_len, head_dim]
+ * with row strides given in elements between consecutive positions
+ * (k_seq_stride) and heads (k_head_stride), batches (k_batch_stride), so a
+ * slice of a preallocated cache can be passed without a copy.
+ * out: [batch, heads, q_len, head_dim].  head_dim 128, bf16 or fp16.
+ */
+LPC_API int lpc_flash_attention(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                        int heads, int kv_heads, int64_t q_len, int64_t kv_len, int head_dim,
+                        int64_t k_batch_stride, int64_t k_head_stride, int causal, float sm_scale,
+                        int dtype, void* stream);
+
+/*
+ * Split-KV decode attention over ragged per-sequence context lengths
+ * (one query token per sequence).
+ * Replaces: `_flash_decode_kernel` (flash_attention.py:450-710, launched at
+ *           :1161-1197), generalised from one KV_LEN per call to a device
+ *           array of lengths.
+ * q: [batch, heads, head_dim]; caches [max_batch, kv_heads, max_seq_len, head_dim];
+ * seq_lens: int32 [batch] on the device, keys [0, seq_lens[b]) are attended;
+ * out: [batch, heads, head_dim].
+ * workspace: lpc_decode_attention_workspace_bytes(batch, heads, max_seq_len, head_dim)
+ * bytes (per-split partial results).
+ */
+LPC_API int64_t lpc_decode_attention_workspace_bytes(int64_t batch, int heads, int64_t max_seq_len,
+                                             int head_dim);
+LPC_API int lpc_decode_attention(const void* q, const void* key_cache, const void* value_cache,
+                         const int32_t* seq_lens, void* out, void* workspace,
+                         int64_t workspace_bytes, int64_t batch, int heads, int kv_heads,
+                         int head_dim, int64_t max_batch, int64_t max_seq_len, float sm_scale,
+                         int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LPC_B200_H */

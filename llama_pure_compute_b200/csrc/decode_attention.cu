@@ -1,0 +1,429 @@
+// Split-KV decode attention over ragged context lengths (one query per sequence).
+//
+// Semantics: out[b, h] = softmax(q[b, h] . K[b, h/G, :L_b]^T * scale) V[b, h/G, :L_b]
+// with fp32 accumulation -- the bottom-right-aligned causal attention of a
+// single new token over its whole context (tests/test_attention_correctness.py:10-76
+// with q_len = 1; the decode kernel src/llama_pure_compute/triton_kernels/
+// flash_attention.py:450-710).  The reference handles one KV_LEN per call
+// (a constexpr, recompiled per length); here each sequence has its own length
+// L_b = seq_lens[b], read on the device.
+//
+// Decomposition (HBM-streaming, no tensor cores: one query row per KV head
+// gives an arithmetic intensity of ~1 FLOP/byte):
+//   grid (split, kv_head, batch); each CTA owns CHUNK keys of one (b, kv head)
+//   and all G = heads/kv_heads query heads that share them.
+//   warp 4     producer: cp.async.bulk copies of contiguous 32-key K and V
+//              slabs (8 KB each for head_dim 128 bf16) into a 4-stage ring,
+//              completion on mbarriers (tx bytes).
+//   warps 0-3  each takes 8 keys of every slab.  Lane l holds dims
+//              [l*D/32, (l+1)*D/32) of q, K rows and the fp32 output
+//              accumulator.  The 8 partial dot products are reduced across the
+//              warp with a transposing butterfly (9 shuffles for 8 keys), so
+//              lanes 4j..4j+3 end with key j's score; online softmax runs in
+//              the log2 domain (scale * log2 e folded into q).
+//   CTA end    the 4 warps' (max, sum, acc) merge through shared memory; a
+//              sequence with a single split writes its output directly, else
+//              the split's partial goes to the workspace and a small combine
+//              kernel merges the splits.
+#include <atomic>
+
+#include "lpc_common.cuh"
+
+LPC_DECLARE_STATUS(g_decode_status)
+
+unsigned int lpc_status_decode(bool clear) {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_decode_status, sizeof(v));
+  if (clear && v) {
+    unsigned int z = 0;
+    cudaMemcpyToSymbol(g_decode_status, &z, sizeof(z));
+  }
+  return v;
+}
+
+namespace {
+
+using lpc::Num;
+
+constexpr int CHUNK = 256;   // keys per split
+constexpr int TILE = 32;     // keys per pipeline stage
+constexpr int NSTAGE = 4;
+constexpr int NCWARPS = 4;   // compute warps
+constexpr int KPW = TILE / NCWARPS;  // keys per warp per stage = 8
+constexpr float LOG2E = 1.4426950408889634f;
+
+// Hardware base-2 exponential (MUFU ex2, approximate, flush-to-zero).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack2(uint32_t w, float& a, float& b);
+template <>
+__device__ __forceinline__ void unpack2<__nv_bfloat16>(uint32_t w, float& a, float& b) {
+  a = lpc::bf16lo(w);
+  b = lpc::bf16hi(w);
+}
+template <>
+__device__ __forceinline__ void unpack2<__half>(uint32_t w, float& a, float& b) {
+  __half2 h = *reinterpret_cast<__half2*>(&w);
+  float2 f = __half22float2(h);
+  a = f.x;
+  b = f.y;
+}
+
+template <int DPL>
+struct RawRow;  // DPL 16-bit values packed in 32-bit words
+template <>
+struct RawRow<4> {
+  uint32_t w[2];
+  __device__ __forceinline__ void load(const uint8_t* p) {
+    uint2 v = *reinterpret_cast<const uint2*>(p);
+    w[0] = v.x;
+    w[1] = v.y;
+  }
+};
+template <>
+struct RawRow<2> {
+  uint32_t w[1];
+  __device__ __forceinline__ void load(const uint8_t* p) { w[0] = *reinterpret_cast<const uint32_t*>(p); }
+};
+
+template <typename T, int D, int G>
+__global__ void __launch_bounds__((NCWARPS + 1) * 32)
+    decode_split_kernel(const T* __restrict__ q, const T* __restrict__ kc,
+                        const T* __restrict__ vc, const int32_t* __restrict__ seq_lens,
+                        T* __restrict__ out, float* __restrict__ part_o,
+                        float* __restrict__ part_ml, int H, int Hkv, int64_t Smax,
+                        int max_splits, float scale_log2) {
+  constexpr int DPL = D / 32;                    // dims per lane
+  constexpr int ROW_BYTES = D * (int)sizeof(T);
+  constexpr int SLAB = TILE * ROW_BYTES;         // one K or V stage
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint8_t* sK = smem;
+  uint8_t* sV = smem + NSTAGE * SLAB;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 2 * NSTAGE * SLAB);
+  float* red = reinterpret_cast<float*>(smem + 2 * NSTAGE * SLAB + 2 * NSTAGE * 8);
+  // red: [NCWARPS][G][D + 2]
+
+  const int split = blockIdx.x;
+  const int kvh = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  int L = __ldg(seq_lens + b);
+  if (L > Smax) {  // never read past this sequence's cache rows
+    if (split == 0 && threadIdx.x == 0) atomicOr(&g_decode_status, LPC_DEV_ERR_BOUNDS);
+    L = (int)Smax;
+  }
+  const int start = split * CHUNK;
+  if (start >= L) return;  // uniform for the whole CTA, before any barrier
+  const int end = min(start + CHUNK, L);
+  const int ntiles = (end - start + TILE - 1) / TILE;
+  const int nsplits = (L + CHUNK - 1) / CHUNK;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  auto full_bar = [&](int s) { return lpc::smem_u32(bar + s); };
+  auto empty_bar = [&](int s) { return lpc::smem_u32(bar + NSTAGE + s); };
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NSTAGE; ++s) {
+      lpc::mbar_init(full_bar(s), 1);
+      lpc::mbar_init(empty_bar(s), NCWARPS);
+    }
+    lpc::fence_mbar_init();
+  }
+  __syncthreads();
+
+  const int64_t head_base = ((b * Hkv + kvh) * Smax) * D;  // elements
+  float m_run[G], l_run[G], acc[G][DPL];
+
+  if (warp == NCWARPS) {
+    if (lane == 0) {
+      for (int t = 0; t < ntiles; ++t) {
+        const int s = t % NSTAGE;
+        const uint32_t r = (uint32_t)(t / NSTAGE);
+        if (!lpc::mbar_wait(empty_bar(s), (r & 1u) ^ 1u, &g_decode_status)) break;
+        const int k0 = start + t * TILE;
+        const uint32_t bytes = (uint32_t)(min(TILE, end - k0) * ROW_BYTES);
+        lpc::mbar_arrive_expect_tx(full_bar(s), 2 * bytes);
+        lpc::bulk_g2s(lpc::smem_u32(sK + s * SLAB), kc + head_base + (int64_t)k0 * D, bytes,
+                      full_bar(s));
+        lpc::bulk_g2s(lpc::smem_u32(sV + s * SLAB), vc + head_base + (int64_t)k0 * D, bytes,
+                      full_bar(s));
+      }
+    }
+  } else {
+    float qf[G][DPL];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const T* qp = q + (b * H + (int64_t)kvh * G + g) * D + lane * DPL;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) qf[g][i] = Num<T>::to_f(qp[i]) * scale_log2;
+      m_run[g] = -INFINITY;
+      l_run[g] = 0.f;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[g][i] = 0.f;
+    }
+    const int my_key = lane >> 2;  // key (within this warp's 8) whose score this lane ends with
+    for (int t = 0; t < ntiles; ++t) {
+      const int s = t % NSTAGE;
+      if (!lpc::mbar_wait(full_bar(s), (uint32_t)(t / NSTAGE) & 1u, &g_decode_status)) break;
+      const int k0 = start + t * TILE;
+      const int nvalid = min(TILE, end - k0) - warp * KPW;  // valid keys for this warp (may be <= 0)
+      RawRow<DPL> kr[KPW], vr[KPW];
+      const uint8_t* kb = sK + s * SLAB + (warp * KPW) * ROW_BYTES + lane * DPL * 2;
+      const uint8_t* vb = sV + s * SLAB + (warp * KPW) * ROW_BYTES + lane * DPL * 2;
+#pragma unroll
+      for (int j = 0; j < KPW; ++j) {
+        if (j < nvalid) {
+          kr[j].load(kb + j * ROW_BYTES);
+          vr[j].load(vb + j * ROW_BYTES);
+        } else {
+#pragma unroll
+          for (int w = 0; w < DPL / 2; ++w) { kr[j].w[w] = 0u; vr[j].w[w] = 0u; }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) lpc::mbar_arrive(empty_bar(s));
+
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float p8[KPW];
+#pragma unroll
+        for (int j = 0; j < KPW; ++j) {
+          float acc_d = 0.f;
+#pragma unroll
+          for (int w = 0; w < DPL / 2; ++w) {
+            float a, c;
+            unpack2<T>(kr[j].w[w], a, c);
+            acc_d = fmaf(qf[g][2 * w], a, acc_d);
+            acc_d = fmaf(qf[g][2 * w + 1], c, acc_d);
+          }
+          p8[j] = acc_d;
+        }
+        // transposing butterfly: 8 keys x 32 lanes -> lanes 4j..4j+3 hold key j
+        {
+          const bool hi = lane & 16;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float send = hi ? p8[j] : p8[j + 4];
+            const float keep = hi ? p8[j + 4] : p8[j];
+            p8[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+          }
+        }
+        {
+          const bool hi = lane & 8;
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const float send = hi ? p8[j] : p8[j + 2];
+            const float keep = hi ? p8[j + 2] : p8[j];
+            p8[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+          }
+        }
+        float sc;
+        {
+          const bool hi = lane & 4;
+          const float send = hi ? p8[0] : p8[1];
+          const float keep = hi ? p8[1] : p8[0];
+          sc = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+        }
+        sc += __shfl_xor_sync(0xffffffffu, sc, 2);
+        sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+        if (my_key >= nvalid) sc = -INFINITY;
+        float mx = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float m_new = fmaxf(m_run[g], mx);
+        const float m_use = m_new == -INFINITY ? 0.f : m_new;
+        const float alpha = fast_exp2(m_run[g] - m_use);
+        const float p = fast_exp2(sc - m_use);
+        m_run[g] = m_new;
+        l_run[g] = l_run[g] * alpha + p;  // per-lane partial (lanes of one key group agree)
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[g][i] *= alpha;
+#pragma unroll
+        for (int j = 0; j < KPW; ++j) {
+          const float pj = __shfl_sync(0xffffffffu, p, 4 * j);
+#pragma unroll
+          for (int w = 0; w < DPL / 2; ++w) {
+            float a, c;
+            unpack2<T>(vr[j].w[w], a, c);
+            acc[g][2 * w] = fmaf(pj, a, acc[g][2 * w]);
+            acc[g][2 * w + 1] = fmaf(pj, c, acc[g][2 * w + 1]);
+          }
+        }
+      }
+    }
+    // per-warp totals: l over the 8 key groups
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float l = l_run[g];
+      l += __shfl_xor_sync(0xffffffffu, l, 4);
+      l += __shfl_xor_sync(0xffffffffu, l, 8);
+      l += __shfl_xor_sync(0xffffffffu, l, 16);
+      float* r = red + (warp * G + g) * (D + 2);
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) r[lane * DPL + i] = acc[g][i];
+      if (lane == 0) {
+        r[D] = m_run[g];
+        r[D + 1] = l;
+      }
+    }
+  }
+  __syncthreads();
+  // merge the 4 warps; threads 0..D-1 each own one output dim per query head
+  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    const int g = idx / D, d = idx - g * D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NCWARPS; ++w) M = fmaxf(M, red[(w * G + g) * (D + 2) + D]);
+    const float Mu = M == -INFINITY ? 0.f : M;
+    float O = 0.f, Ls = 0.f;
+#pragma unroll
+    for (int w = 0; w < NCWARPS; ++w) {
+      const float* r = red + (w * G + g) * (D + 2);
+      const float f = fast_exp2(r[D] - Mu);
+      O = fmaf(f, r[d], O);
+      Ls = fmaf(f, r[D + 1], Ls);
+    }
+    const int h = kvh * G + g;
+    if (nsplits == 1) {
+      out[(b * H + h) * D + d] = Num<T>::from_f(Ls > 0.f ? O / Ls : 0.f);
+    } else {
+      const int64_t pi = (b * H + h) * (int64_t)max_splits + split;
+      part_o[pi * D + d] = O;
+      if (d == 0) {
+        part_ml[2 * pi] = M;
+        part_ml[2 * pi + 1] = Ls;
+      }
+    }
+  }
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(D) decode_combine_kernel(const float* __restrict__ part_o,
+                                                          const float* __restrict__ part_ml,
+                                                          const int32_t* __restrict__ seq_lens,
+                                                          T* __restrict__ out, int H,
+                                                          int max_splits, int64_t Smax) {
+  const int64_t bh = blockIdx.x;
+  const int64_t b = bh / H;
+  const int L = min((int64_t)__ldg(seq_lens + b), Smax);
+  const int d = threadIdx.x;
+  if (L <= 0) {
+    out[bh * D + d] = Num<T>::from_f(0.f);
+    return;
+  }
+  const int ns = (L + CHUNK - 1) / CHUNK;
+  if (ns <= 1) return;  // written by the split kernel
+  const float* ml = part_ml + bh * max_splits * 2;
+  float M = -INFINITY;
+  for (int s = 0; s < ns; ++s) M = fmaxf(M, ml[2 * s]);
+  const float Mu = M == -INFINITY ? 0.f : M;
+  float O = 0.f, Ls = 0.f;
+  const float* po = part_o + bh * max_splits * D;
+  for (int s = 0; s < ns; ++s) {
+    const float f = fast_exp2(ml[2 * s] - Mu);
+    O = fmaf(f, po[s * D + d], O);
+    Ls = fmaf(f, ml[2 * s + 1], Ls);
+  }
+  out[bh * D + d] = Num<T>::from_f(Ls > 0.f ? O / Ls : 0.f);
+}
+
+template <typename T, int D, int G>
+int launch_g(const void* q, const void* kc, const void* vc, const int32_t* lens, void* out,
+             float* po, float* pml, int64_t B, int H, int Hkv, int64_t Smax, int max_splits,
+             float scale_log2, cudaStream_t s) {
+  constexpr int SLAB = TILE * D * 2;
+  const int smem = 2 * NSTAGE * SLAB + 2 * NSTAGE * 8 + NCWARPS * G * (D + 2) * 4;
+  static std::atomic<uint64_t> mask{0};
+  int rc = lpc::once_per_device_smem((const void*)decode_split_kernel<T, D, G>, smem, mask);
+  if (rc) return rc;
+  dim3 grid((unsigned)max_splits, (unsigned)Hkv, (unsigned)B);
+  decode_split_kernel<T, D, G><<<grid, (NCWARPS + 1) * 32, smem, s>>>(
+      (const T*)q, (const T*)kc, (const T*)vc, lens, (T*)out, po, pml, H, Hkv, Smax, max_splits,
+      scale_log2);
+  if ((rc = lpc::check_launch("decode_attention (split)"))) return rc;
+  decode_combine_kernel<T, D><<<(unsigned)(B * H), D, 0, s>>>(po, pml, lens, (T*)out, H,
+                                                              max_splits, Smax);
+  return lpc::check_launch("decode_attention (combine)");
+}
+
+template <typename T, int D>
+int launch_d(int G, const void* q, const void* kc, const void* vc, const int32_t* lens,
+             void* out, float* po, float* pml, int64_t B, int H, int Hkv, int64_t Smax,
+             int max_splits, float sl2, cudaStream_t s) {
+  switch (G) {
+    case 1: return launch_g<T, D, 1>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, sl2, s);
+    case 2: return launch_g<T, D, 2>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, sl2, s);
+    case 4: return launch_g<T, D, 4>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, sl2, s);
+    case 8: return launch_g<T, D, 8>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, sl2, s);
+  }
+  lpc::set_error("decode_attention: heads/kv_heads = %d not supported (1, 2, 4 or 8)", G);
+  return LPC_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+
+extern "C" int64_t lpc_decode_attention_workspace_bytes(int64_t batch, int heads,
+                                                        int64_t max_seq_len, int head_dim) {
+  if (batch <= 0 || heads <= 0 || max_seq_len <= 0 || head_dim <= 0) return 0;
+  const int64_t max_splits = (max_seq_len + CHUNK - 1) / CHUNK;
+  return batch * heads * max_splits * (int64_t)(head_dim + 2) * 4;
+}
+
+extern "C" int lpc_decode_attention(const void* q, const void* key_cache, const void* value_cache,
+                                    const int32_t* seq_lens, void* out, void* workspace,
+                                    int64_t workspace_bytes, int64_t batch, int heads,
+                                    int kv_heads, int head_dim, int64_t max_batch,
+                                    int64_t max_seq_len, float sm_scale, int dtype,
+                                    void* stream) {
+  using namespace lpc;
+  if (batch < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || max_batch <= 0 ||
+      max_seq_len <= 0 || batch > max_batch) {
+    set_error("decode_attention: invalid sizes (batch=%lld heads=%d kv_heads=%d max_batch=%lld)",
+              (long long)batch, heads, kv_heads, (long long)max_batch);
+    return LPC_ERR_INVALID;
+  }
+  if (batch == 0) return LPC_OK;
+  if (dtype != LPC_DTYPE_BF16 && dtype != LPC_DTYPE_F16) {
+    set_error("decode_attention: only bf16 and fp16 are supported");
+    return LPC_ERR_UNSUPPORTED;
+  }
+  if (head_dim != 128 && head_dim != 64) {
+    set_error("decode_attention: head_dim must be 64 or 128, got %d", head_dim);
+    return LPC_ERR_UNSUPPORTED;
+  }
+  if (!q || !key_cache || !value_cache || !seq_lens || !out) {
+    set_error("decode_attention: null pointer");
+    return LPC_ERR_INVALID;
+  }
+  if (!aligned16(key_cache) || !aligned16(value_cache) || !aligned16(q) || !aligned16(out)) {
+    set_error("decode_attention: tensors must be 16-byte aligned");
+    return LPC_ERR_INVALID;
+  }
+  const int64_t need = lpc_decode_attention_workspace_bytes(batch, heads, max_seq_len, head_dim);
+  if (!workspace || workspace_bytes < need || !aligned16(workspace)) {
+    set_error("decode_attention: workspace of %lld bytes required, got %lld", (long long)need,
+              (long long)workspace_bytes);
+    return LPC_ERR_INVALID;
+  }
+  const int64_t max_splits = (max_seq_len + CHUNK - 1) / CHUNK;
+  if (max_splits > 65535 || batch > 65535 || kv_heads > 65535) {
+    set_error("decode_attention: grid too large");
+    return LPC_ERR_UNSUPPORTED;
+  }
+  float* po = static_cast<float*>(workspace);
+  float* pml = po + batch * heads * max_splits * head_dim;
+  const float sl2 = sm_scale * LOG2E;
+  const int G = heads / kv_heads;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == LPC_DTYPE_BF16) {
+    if (head_dim == 128)
+      return launch_d<__nv_bfloat16, 128>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, (int)max_splits, sl2, s);
+    return launch_d<__nv_bfloat16, 64>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, (int)max_splits, sl2, s);
+  }
+  if (head_dim == 128)
+    return launch_d<__half, 128>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, (int)max_splits, sl2, s);
+  return launch_d<__half, 64>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, (int)max_splits, sl2, s);
+}

@@ -1,0 +1,441 @@
+// Flash attention for prefill on tcgen05 tensor cores (sm_100a).
+//
+// out = softmax(Q K^T * scale + mask) V, fp32 accumulation, queries aligned to
+// the end of the keys (bottom-right causal mask: query row r of a q_len-row
+// block attends keys <= kv_len - q_len + r), as in
+// tests/test_attention_correctness.py:10-76 and the causal prefill kernel of
+// src/llama_pure_compute/triton_kernels/flash_attention.py:88-432.
+//
+// One CTA per (128-query tile, head, batch); 6 warps:
+//   warp 4     TMA producer: Q tile once (two 64-column boxes), then K and V
+//              128-key tiles into 2-stage rings, 4-D tensor maps so rows past
+//              kv_len (or q_len) read as zeros.
+//   warp 5     TMEM allocator and single-thread tcgen05.mma issuer:
+//                S_j = Q K_j^T           (M=128, N=128, K=128: 8 instructions)
+//                O  += P_{j-1} V_{j-1}   (A = P from smem, B = V MN-major)
+//              S is double-buffered in TMEM so S_{j+1} runs while the softmax
+//              warps work on S_j.
+//   warps 0-3  softmax: thread r owns query row r (TMEM lane r).  Row max and
+//              exp2 in fp32 from tcgen05.ld of S; P rounded to bf16/fp16 and
+//              written into a 128-byte-swizzled smem tile that is the A operand
+//              of the PV MMA.  The running max only moves (and O in TMEM is
+//              rescaled) when a tile's max exceeds it by more than 2^8, so the
+//              O correction is rare; the result is the same softmax, only the
+//              reference point of the exponentials differs.  Epilogue: O / l.
+// TMEM: S0 cols [0,128), S1 [128,256), O [256,384) (512 allocated).
+// Causal tiles past the diagonal are skipped entirely; q tiles are scheduled
+// longest-first.
+#include <atomic>
+
+#include "lpc_common.cuh"
+
+LPC_DECLARE_STATUS(g_prefill_status)
+
+unsigned int lpc_status_prefill(bool clear) {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_prefill_status, sizeof(v));
+  if (clear && v) {
+    unsigned int z = 0;
+    cudaMemcpyToSymbol(g_prefill_status, &z, sizeof(z));
+  }
+  return v;
+}
+
+namespace {
+
+constexpr int BQ = 128;       // queries per CTA (UMMA M)
+constexpr int BKV = 128;      // keys per tile (UMMA N of S, K of PV)
+constexpr int HD = 128;       // head dim
+constexpr int BOX = 64;       // 64 x 2 B = one 128-byte swizzle row
+constexpr int TILE_BYTES = BQ * HD * 2;          // 32 KB: Q, one K stage, one V stage, P
+constexpr int HALF_BYTES = TILE_BYTES / 2;       // one 64-column box
+constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 256;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float RESCALE_THRESHOLD = 8.0f;        // log2 units
+
+struct TmaDesc4 { alignas(64) unsigned char bytes[128]; };
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int c0, int c1, int c2,
+                                            int c3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+struct Params {
+  int64_t q_len, kv_len, offset;  // offset = kv_len - q_len
+  int heads, kv_heads, group, num_q_tiles;
+  float scale_log2;
+  int causal;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(192, 1)
+    flash_prefill_kernel(const __grid_constant__ TmaDesc4 tmQ, const __grid_constant__ TmaDesc4 tmK,
+                         const __grid_constant__ TmaDesc4 tmV, T* __restrict__ out,
+                         const Params p, uint32_t idesc_qk, uint32_t idesc_pv) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = lpc::smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t sQ = base;
+  const uint32_t sK = base + TILE_BYTES;          // 2 stages
+  const uint32_t sV = base + 3 * TILE_BYTES;      // 2 stages
+  const uint32_t sP = base + 5 * TILE_BYTES;
+  const uint32_t bars = base + 6 * TILE_BYTES;
+  const uint32_t q_full = bars + 0;
+  auto k_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto k_empty = [&](int s) { return bars + 8u * (3 + s); };
+  auto v_full = [&](int s) { return bars + 8u * (5 + s); };
+  auto v_empty = [&](int s) { return bars + 8u * (7 + s); };
+  auto s_full = [&](int s) { return bars + 8u * (9 + s); };
+  auto s_empty = [&](int s) { return bars + 8u * (11 + s); };
+  const uint32_t p_full = bars + 8u * 13;
+  const uint32_t o_ready = bars + 8u * 14;
+  const uint32_t tmem_slot = bars + 8u * 15;
+  volatile uint32_t* tmem_slot_ptr =
+      reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = p.num_q_tiles - 1 - (int)blockIdx.x;  // longest causal rows first
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int kvh = h / p.group;
+  const int64_t q0 = (int64_t)qt * BQ;
+  const int64_t kv_tiles_all = (p.kv_len + BKV - 1) / BKV;
+  int64_t n_tiles = kv_tiles_all;
+  if (p.causal) {
+    const int64_t last_key = p.offset + q0 + BQ - 1;  // largest key any row of this tile may see
+    n_tiles = min(n_tiles, last_key / BKV + 1);
+  }
+  const int n = (int)n_tiles;
+
+  if (threadIdx.x == 0) {
+    lpc::mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      lpc::mbar_init(k_full(s), 1);
+      lpc::mbar_init(k_empty(s), 1);
+      lpc::mbar_init(v_full(s), 1);
+      lpc::mbar_init(v_empty(s), 1);
+      lpc::mbar_init(s_full(s), 1);
+      lpc::mbar_init(s_empty(s), 4);
+    }
+    lpc::mbar_init(p_full, 4);
+    lpc::mbar_init(o_ready, 1);
+    lpc::fence_mbar_init();
+  }
+  if (warp == 4 && lane == 0) {
+    lpc::tma_prefetch_desc(&tmQ);
+    lpc::tma_prefetch_desc(&tmK);
+    lpc::tma_prefetch_desc(&tmV);
+  }
+  if (warp == 5) {
+    lpc::tmem_alloc(tmem_slot, TMEM_COLS);
+    lpc::tmem_relinquish();
+  }
+  lpc::tc_fence_before();
+  __syncthreads();
+  lpc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot_ptr;
+  const uint32_t tO = tmem + 256u;
+  unsigned int* st = &g_prefill_status;
+
+  if (warp == 4) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0 && n > 0) {
+      lpc::mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      tma_load_4d(sQ, &tmQ, 0, (int)q0, h, b, q_full);
+      tma_load_4d(sQ + HALF_BYTES, &tmQ, BOX, (int)q0, h, b, q_full);
+      for (int j = 0; j < n; ++j) {
+        const int s = j & 1;
+        const uint32_t par = ((uint32_t)(j >> 1) & 1u) ^ 1u;
+        const int k0 = j * BKV;
+        if (!lpc::mbar_wait(k_empty(s), par, st)) break;
+        lpc::mbar_arrive_expect_tx(k_full(s), TILE_BYTES);
+        tma_load_4d(sK + s * TILE_BYTES, &tmK, 0, k0, kvh, b, k_full(s));
+        tma_load_4d(sK + s * TILE_BYTES + HALF_BYTES, &tmK, BOX, k0, kvh, b, k_full(s));
+        if (!lpc::mbar_wait(v_empty(s), par, st)) break;
+        lpc::mbar_arrive_expect_tx(v_full(s), TILE_BYTES);
+        tma_load_4d(sV + s * TILE_BYTES, &tmV, 0, k0, kvh, b, v_full(s));
+        tma_load_4d(sV + s * TILE_BYTES + HALF_BYTES, &tmV, BOX, k0, kvh, b, v_full(s));
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && n > 0) {
+      bool ok = lpc::mbar_wait(q_full, 0, st);
+      auto do_pv = [&](int i) -> bool {
+        if (!lpc::mbar_wait(p_full, (uint32_t)i & 1u, st)) return false;
+        if (!lpc::mbar_wait(v_full(i & 1), (uint32_t)(i >> 1) & 1u, st)) return false;
+        lpc::tc_fence_after();
+        const uint32_t vb = sV + (i & 1) * TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          // A: P rows = queries, K = keys (K-major, two 64-key boxes)
+          const uint64_t ad =
+              lpc::smem_desc_sw128(sP + (kk >> 2) * HALF_BYTES, 16, 1024) + 2u * (kk & 3);
+          // B: V rows = keys (K), 64-dim boxes along N: LBO = box stride, SBO = 8 keys
+          const uint64_t bd = lpc::smem_desc_sw128(vb + kk * 16 * 128, HALF_BYTES, 1024);
+          lpc::umma_ss(tO, ad, bd, idesc_pv, (i | kk) != 0);
+        }
+        lpc::umma_commit(v_empty(i & 1));
+        lpc::umma_commit(o_ready);
+        return true;
+      };
+      for (int j = 0; j < n && ok; ++j) {
+        const int s = j & 1;
+        if (!lpc::mbar_wait(k_full(s), (uint32_t)(j >> 1) & 1u, st)) { ok = false; break; }
+        if (j >= 2 && !lpc::mbar_wait(s_empty(s), (uint32_t)((j - 2) >> 1) & 1u, st)) { ok = false; break; }
+        lpc::tc_fence_after();
+        const uint32_t kb = sK + s * TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint64_t ad =
+              lpc::smem_desc_sw128(sQ + (kk >> 2) * HALF_BYTES, 16, 1024) + 2u * (kk & 3);
+          const uint64_t bd =
+              lpc::smem_desc_sw128(kb + (kk >> 2) * HALF_BYTES, 16, 1024) + 2u * (kk & 3);
+          lpc::umma_ss((tmem + 128u * (uint32_t)s), ad, bd, idesc_qk, kk != 0);
+        }
+        lpc::umma_commit(s_full(s));
+        lpc::umma_commit(k_empty(s));
+        if (j >= 1 && !do_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok) do_pv(n - 1);
+    }
+  } else {
+    // ---------------- softmax + epilogue (warps 0-3) ----------------
+    const int r = warp * 32 + lane;          // query row within the tile
+    const int64_t qpos = p.offset + q0 + r;  // absolute position of this query
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = n > 0;
+    for (int j = 0; j < n && ok; ++j) {
+      const int s = j & 1;
+      if (!lpc::mbar_wait(s_full(s), (uint32_t)(j >> 1) & 1u, st)) { ok = false; break; }
+      lpc::tc_fence_after();
+      const int64_t k0 = (int64_t)j * BKV;
+      const bool need_mask = (k0 + BKV > p.kv_len) || (p.causal && k0 + BKV - 1 > p.offset + q0);
+      const int64_t lim = p.causal ? min(qpos, p.kv_len - 1) : p.kv_len - 1;  // last visible key
+      // pass 1: row max
+      float mt = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < BKV; c += 32) {
+        uint32_t v[32];
+        lpc::tmem_ld32((tmem + 128u * (uint32_t)s) + lane_off + c, v);
+        lpc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float x = __uint_as_float(v[i]);
+          if (need_mask && k0 + c + i > lim) x = -INFINITY;
+          mt = fmaxf(mt, x);
+        }
+      }
+      mt *= p.scale_log2;  // scale > 0
+      // wait for PV_{j-1}: P buffer free and O stable
+      if (j >= 1 && !lpc::mbar_wait(o_ready, (uint32_t)(j - 1) & 1u, st)) { ok = false; break; }
+      lpc::tc_fence_after();
+      float alpha = 1.f;
+      bool rescale = false;
+      if (j == 0) {
+        m_used = mt;
+      } else if (mt > m_used + RESCALE_THRESHOLD) {
+        alpha = fast_exp2(m_used - mt);
+        m_used = mt;
+        rescale = true;
+      }
+      const float m_use = m_used == -INFINITY ? 0.f : m_used;
+      // pass 2: P = exp2(S*scale - m), row sum, bf16 P into the swizzled smem tile
+      float rs = 0.f;
+      const uint32_t prow = sP + (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
+#pragma unroll 1
+      for (int c = 0; c < BKV; c += 32) {
+        uint32_t v[32];
+        lpc::tmem_ld32((tmem + 128u * (uint32_t)s) + lane_off + c, v);
+        lpc::tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float x0 = __uint_as_float(v[i]), x1 = __uint_as_float(v[i + 1]);
+          float e0 = fast_exp2(fmaf(x0, p.scale_log2, -m_use));
+          float e1 = fast_exp2(fmaf(x1, p.scale_log2, -m_use));
+          if (need_mask) {
+            if (k0 + c + i > lim) e0 = 0.f;
+            if (k0 + c + i + 1 > lim) e1 = 0.f;
+          }
+          rs += e0 + e1;
+          pk[i >> 1] = pack2<T>(e0, e1);
+        }
+        // 32 keys = 4 chunks of 16 bytes; chunk index within the 64-key box
+        const uint32_t box = sP + (uint32_t)(c >> 6) * HALF_BYTES;
+        const uint32_t rowb = box - sP + prow;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const uint32_t chunk = (uint32_t)((c & 63) >> 3) + q4;
+          const uint32_t addr = rowb + ((chunk ^ (uint32_t)(r & 7)) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * q4]),
+                       "r"(pk[4 * q4 + 1]), "r"(pk[4 * q4 + 2]), "r"(pk[4 * q4 + 3])
+                       : "memory");
+        }
+      }
+      l = l * alpha + rs;
+      lpc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) lpc::mbar_arrive(s_empty(s));
+      // rare: move O to the new reference max (warp-collective TMEM access)
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 16) {
+          uint32_t v[16];
+          lpc::tmem_ld16(tO + lane_off + c, v);
+          lpc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+          lpc::tmem_st16(tO + lane_off + c, v);
+        }
+        lpc::tmem_wait_st();
+      }
+      lpc::fence_proxy_async_smem();
+      lpc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) lpc::mbar_arrive(p_full);
+    }
+    // epilogue: O / l
+    if (ok && lpc::mbar_wait(o_ready, (uint32_t)(n - 1) & 1u, st)) {
+      lpc::tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const bool valid = q0 + r < p.q_len;
+      T* orow = out + (((int64_t)b * p.heads + h) * p.q_len + q0 + r) * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        uint32_t v[32];
+        lpc::tmem_ld32(tO + lane_off + c, v);
+        lpc::tmem_wait_ld();
+        if (valid) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2)
+            pk[i >> 1] = pack2<T>(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv);
+          uint4* dst = reinterpret_cast<uint4*>(orow + c);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+            dst[q4] = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+        }
+      }
+    }
+  }
+  lpc::tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    lpc::tc_fence_after();
+    lpc::tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+extern "C" int lpc_flash_attention(const void* q, const void* k, const void* v, void* out,
+                                   int64_t batch, int heads, int kv_heads, int64_t q_len,
+                                   int64_t kv_len, int head_dim, int64_t k_batch_stride,
+                                   int64_t k_head_stride, int causal, float sm_scale, int dtype,
+                                   void* stream) {
+  using namespace lpc;
+  if (batch <= 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || q_len <= 0 ||
+      kv_len <= 0) {
+    set_error("flash_attention: invalid sizes (batch=%lld heads=%d kv_heads=%d q_len=%lld "
+              "kv_len=%lld)", (long long)batch, heads, kv_heads, (long long)q_len,
+              (long long)kv_len);
+    return LPC_ERR_INVALID;
+  }
+  if (q_len > kv_len) {
+    set_error("flash_attention: Q_LEN cannot exceed KV_LEN.");
+    return LPC_ERR_INVALID;
+  }
+  if (head_dim != HD) {
+    set_error("flash_attention: head_dim %d not supported by the tcgen05 kernel (128)", head_dim);
+    return LPC_ERR_UNSUPPORTED;
+  }
+  if (dtype != LPC_DTYPE_BF16 && dtype != LPC_DTYPE_F16) {
+    set_error("flash_attention: Only FP16 and BF16 are supported.");
+    return LPC_ERR_UNSUPPORTED;
+  }
+  if (!q || !k || !v || !out) {
+    set_error("flash_attention: null pointer");
+    return LPC_ERR_INVALID;
+  }
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) ||
+      k_head_stride < kv_len * head_dim || k_batch_stride < (int64_t)kv_heads * k_head_stride) {
+    set_error("flash_attention: bad alignment or strides");
+    return LPC_ERR_INVALID;
+  }
+  if (batch > 65535 || heads > 65535 || q_len > 0x7fffffffLL || kv_len > 0x7fffffffLL) {
+    set_error("flash_attention: sizes exceed the launch grid");
+    return LPC_ERR_UNSUPPORTED;
+  }
+  TmaDesc4 tq, tk, tv;
+  const uint64_t rowb = (uint64_t)head_dim * 2;
+  {
+    uint64_t dims[4] = {(uint64_t)head_dim, (uint64_t)q_len, (uint64_t)heads, (uint64_t)batch};
+    uint64_t str[3] = {rowb, rowb * q_len, rowb * q_len * heads};
+    uint32_t box[4] = {BOX, BQ, 1, 1};
+    int rc = make_tma_nd(reinterpret_cast<TmaDesc*>(&tq), q, dtype, 4, dims, str, box, true);
+    if (rc) return rc;
+  }
+  {
+    uint64_t dims[4] = {(uint64_t)head_dim, (uint64_t)kv_len, (uint64_t)kv_heads, (uint64_t)batch};
+    uint64_t str[3] = {rowb, (uint64_t)k_head_stride * 2, (uint64_t)k_batch_stride * 2};
+    uint32_t box[4] = {BOX, BKV, 1, 1};
+    int rc = make_tma_nd(reinterpret_cast<TmaDesc*>(&tk), k, dtype, 4, dims, str, box, true);
+    if (rc) return rc;
+    rc = make_tma_nd(reinterpret_cast<TmaDesc*>(&tv), v, dtype, 4, dims, str, box, true);
+    if (rc) return rc;
+  }
+  Params p;
+  p.q_len = q_len;
+  p.kv_len = kv_len;
+  p.offset = kv_len - q_len;
+  p.heads = heads;
+  p.kv_heads = kv_heads;
+  p.group = heads / kv_heads;
+  p.num_q_tiles = (int)((q_len + BQ - 1) / BQ);
+  p.scale_log2 = sm_scale * LOG2E;
+  p.causal = causal ? 1 : 0;
+  const uint32_t fmt = dtype == LPC_DTYPE_BF16 ? 1u : 0u;
+  const uint32_t id_qk = idesc_f16(fmt, BQ, BKV, 0u, 0u);
+  const uint32_t id_pv = idesc_f16(fmt, BQ, HD, 0u, 1u);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  dim3 grid((unsigned)p.num_q_tiles, (unsigned)heads, (unsigned)batch);
+  int rc;
+  if (dtype == LPC_DTYPE_BF16) {
+    static std::atomic<uint64_t> mask{0};
+    if ((rc = once_per_device_smem((const void*)flash_prefill_kernel<__nv_bfloat16>, SMEM_BYTES, mask)))
+      return rc;
+    flash_prefill_kernel<__nv_bfloat16><<<grid, 192, SMEM_BYTES, s>>>(tq, tk, tv, (__nv_bfloat16*)out, p, id_qk, id_pv);
+  } else {
+    static std::atomic<uint64_t> mask{0};
+    if ((rc = once_per_device_smem((const void*)flash_prefill_kernel<__half>, SMEM_BYTES, mask)))
+      return rc;
+    flash_prefill_kernel<__half><<<grid, 192, SMEM_BYTES, s>>>(tq, tk, tv, (__half*)out, p, id_qk, id_pv);
+  }
+  return check_launch("flash_attention");
+}

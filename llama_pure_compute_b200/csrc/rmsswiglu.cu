@@ -1,0 +1,412 @@
+// Fused RMSNorm + SwiGLU: out = silu(norm(x) Wg^T) * (norm(x) Wu^T).
+//
+// Semantics follow `_rmsswiglu_forward_pytorch` (src/llama_pure_compute/ops.py:45-59)
+// and the reference CUDA op (src/csrc/ops/rmsswiglu.cu:151-282), including the
+// pre-fused weight form (up_w empty: gate_w is [2*inter, dim], gate rows first,
+// rmsswiglu.cu:167-173).  The reference runs three launches with a
+// [tokens, 2*inter] HBM round trip and a per-call torch::cat of the weights;
+// here the gate/up products never leave the chip.
+//
+// bf16/fp16 path (tensor cores, sm_100a):
+//   1. row RMSNorm -> normalised activations in the caller's workspace (bf16)
+//   2. one warp-specialised tcgen05 GEMM per 128-token x 64-inter tile:
+//        warp 4     TMA producer: A = 128x64 activation tile, B = 64 gate rows
+//                   + 64 up rows (two TMA boxes into one 128-row operand)
+//        warp 5     TMEM allocator + single-thread tcgen05.mma issuer
+//                   (M=128, N=128, K=16 per instruction, fp32 accumulators)
+//        warps 0-3  epilogue: tcgen05.ld the gate and up columns of each token
+//                   row, silu(g)*u in fp32, one rounding to the output dtype
+//      6-stage smem ring, 32 KB per stage, mbarrier full/empty handshakes.
+//      Tiles are rasterised in groups of GROUP_M token tiles so that a wave of
+//      CTAs re-reads weight tiles from L2 rather than HBM.
+// fp32 path (CUDA cores, no TF32): each CTA normalises up to 8 token rows into
+//   shared memory, then streams gate/up rows with 16-byte loads and reduces the
+//   dot products per warp.  It is the weight-streaming (HBM-bound) GEMV of the
+//   fp32 op shape (8 tokens).
+#include <atomic>
+#include <mutex>
+
+#include "lpc_common.cuh"
+
+LPC_DECLARE_STATUS(g_swiglu_status)
+
+unsigned int lpc_status_swiglu(bool clear) {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_swiglu_status, sizeof(v));
+  if (clear && v) {
+    unsigned int z = 0;
+    cudaMemcpyToSymbol(g_swiglu_status, &z, sizeof(z));
+  }
+  return v;
+}
+
+int lpc_rmsnorm_launch(const void* x, const void* w, void* y, int64_t rows, int dim, float eps,
+                       int dtype, int w_dtype, cudaStream_t s);
+
+namespace {
+
+using lpc::Num;
+
+constexpr int BM = 128;          // tokens per tile (UMMA M)
+constexpr int BNI = 64;          // inter columns per tile
+constexpr int BN = 2 * BNI;      // UMMA N: 64 gate rows + 64 up rows
+constexpr int BK = 64;           // 64 x 2 B = one 128-byte swizzle row
+constexpr int STAGES = 6;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TC_SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int GROUP_M = 16;
+constexpr uint32_t TMEM_COLS = 128;
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  return __fdividef(g, 1.0f + __expf(-g)) * u;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(192, 1)
+    swiglu_tc_kernel(const __grid_constant__ lpc::TmaDesc tmA,
+                     const __grid_constant__ lpc::TmaDesc tmG,
+                     const __grid_constant__ lpc::TmaDesc tmU, T* __restrict__ out, int M, int K,
+                     int I, int up_row_off, int num_m, int num_n, uint32_t idesc) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = lpc::smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t sA = base;
+  const uint32_t sB = base + STAGES * A_BYTES;
+  const uint32_t bars = sB + STAGES * B_BYTES;
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
+  const uint32_t accum_bar = bars + 8u * (2 * STAGES);
+  const uint32_t tmem_slot = bars + 8u * (2 * STAGES + 1);
+  volatile uint32_t* tmem_slot_ptr =
+      reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // grouped rasterisation: GROUP_M token tiles sweep all inter tiles together
+  const int bid = blockIdx.x;
+  const int group = bid / (GROUP_M * num_n);
+  const int first_m = group * GROUP_M;
+  const int gm = min(GROUP_M, num_m - first_m);
+  const int within = bid - group * GROUP_M * num_n;
+  const int mt = first_m + within % gm;
+  const int nt = within / gm;
+  const int m0 = mt * BM, i0 = nt * BNI;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      lpc::mbar_init(full_bar(s), 1);
+      lpc::mbar_init(empty_bar(s), 1);
+    }
+    lpc::mbar_init(accum_bar, 1);
+    lpc::fence_mbar_init();
+  }
+  if (warp == 4 && lane == 0) {
+    lpc::tma_prefetch_desc(&tmA);
+    lpc::tma_prefetch_desc(&tmG);
+    lpc::tma_prefetch_desc(&tmU);
+  }
+  if (warp == 5) {
+    lpc::tmem_alloc(tmem_slot, TMEM_COLS);
+    lpc::tmem_relinquish();
+  }
+  lpc::tc_fence_before();
+  __syncthreads();
+  lpc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot_ptr;
+  const int nkb = K / BK;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t r = (uint32_t)(kb / STAGES);
+        if (!lpc::mbar_wait(empty_bar(s), (r & 1u) ^ 1u, &g_swiglu_status)) break;
+        lpc::mbar_arrive_expect_tx(full_bar(s), STAGE_BYTES);
+        lpc::tma_load_2d(sA + s * A_BYTES, &tmA, kb * BK, m0, full_bar(s));
+        lpc::tma_load_2d(sB + s * B_BYTES, &tmG, kb * BK, i0, full_bar(s));
+        lpc::tma_load_2d(sB + s * B_BYTES + B_BYTES / 2, &tmU, kb * BK, i0 + up_row_off,
+                         full_bar(s));
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t r = (uint32_t)(kb / STAGES);
+        if (!lpc::mbar_wait(full_bar(s), r & 1u, &g_swiglu_status)) break;
+        lpc::tc_fence_after();
+        const uint64_t ad = lpc::smem_desc_sw128(sA + s * A_BYTES, 16, 1024);
+        const uint64_t bd = lpc::smem_desc_sw128(sB + s * B_BYTES, 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          lpc::umma_ss(tmem, ad + 2u * kk, bd + 2u * kk, idesc, (kb | kk) != 0);
+        lpc::umma_commit(empty_bar(s));
+      }
+      lpc::umma_commit(accum_bar);
+    }
+  } else {
+    // epilogue warps 0..3: TMEM lanes 32*warp .. 32*warp+31 = token rows
+    const bool ok = lpc::mbar_wait(accum_bar, 0, &g_swiglu_status);
+    lpc::tc_fence_after();
+    const int row = m0 + warp * 32 + lane;
+    const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
+    if (ok) {
+#pragma unroll 1
+      for (int c = 0; c < BNI; c += 16) {
+        uint32_t g[16], u[16];
+        lpc::tmem_ld16(taddr + c, g);
+        lpc::tmem_ld16(taddr + BNI + c, u);
+        lpc::tmem_wait_ld();
+        if (row < M && i0 + c < I) {
+          uint32_t p[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            p[j] = pack2<T>(silu_mul(__uint_as_float(g[2 * j]), __uint_as_float(u[2 * j])),
+                            silu_mul(__uint_as_float(g[2 * j + 1]), __uint_as_float(u[2 * j + 1])));
+          uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)row * I + i0 + c);
+          dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
+          dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
+        }
+      }
+    }
+  }
+  lpc::tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    lpc::tc_fence_after();
+    lpc::tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// fp32 streaming path
+// ---------------------------------------------------------------------------
+constexpr int F32_ROWS = 8;
+constexpr int F32_WARPS = 8;
+
+template <typename W>
+__global__ void __launch_bounds__(F32_WARPS * 32, 1)
+    swiglu_f32_kernel(const float* __restrict__ x, const W* __restrict__ nw,
+                      const float* __restrict__ wg, const float* __restrict__ wu,
+                      float* __restrict__ out, int64_t M, int K, int I, float eps) {
+  extern __shared__ float4 xs4[];  // [F32_ROWS][K/4]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t m0 = (int64_t)blockIdx.y * F32_ROWS;
+  const int rows = (int)min((int64_t)F32_ROWS, M - m0);
+  const int kv = K >> 2;
+
+  // prologue: RMSNorm of this CTA's token rows into shared memory
+  for (int r = warp; r < F32_ROWS; r += F32_WARPS) {
+    float4* dst = xs4 + (int64_t)r * kv;
+    if (r < rows) {
+      const float4* src = reinterpret_cast<const float4*>(x + (m0 + r) * K);
+      float ss = 0.f;
+      for (int v = lane; v < kv; v += 32) {
+        const float4 a = __ldg(src + v);
+        ss = fmaf(a.x, a.x, ss);
+        ss = fmaf(a.y, a.y, ss);
+        ss = fmaf(a.z, a.z, ss);
+        ss = fmaf(a.w, a.w, ss);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float rr = rsqrtf(ss / (float)K + eps);
+      for (int v = lane; v < kv; v += 32) {
+        const float4 a = __ldg(src + v);
+        float4 o;
+        o.x = __fmul_rn(__fmul_rn(a.x, rr), Num<W>::to_f(nw[4 * v + 0]));
+        o.y = __fmul_rn(__fmul_rn(a.y, rr), Num<W>::to_f(nw[4 * v + 1]));
+        o.z = __fmul_rn(__fmul_rn(a.z, rr), Num<W>::to_f(nw[4 * v + 2]));
+        o.w = __fmul_rn(__fmul_rn(a.w, rr), Num<W>::to_f(nw[4 * v + 3]));
+        dst[v] = o;
+      }
+    } else {
+      for (int v = lane; v < kv; v += 32) dst[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  __syncthreads();
+
+  const int gw = blockIdx.x * F32_WARPS + warp;
+  const int nwarps = gridDim.x * F32_WARPS;
+  for (int i = 2 * gw; i < I; i += 2 * nwarps) {
+    const bool two = i + 1 < I;
+    const float4* g0p = reinterpret_cast<const float4*>(wg + (int64_t)i * K);
+    const float4* u0p = reinterpret_cast<const float4*>(wu + (int64_t)i * K);
+    const float4* g1p = two ? g0p + kv : g0p;
+    const float4* u1p = two ? u0p + kv : u0p;
+    float ag0[F32_ROWS], au0[F32_ROWS], ag1[F32_ROWS], au1[F32_ROWS];
+#pragma unroll
+    for (int r = 0; r < F32_ROWS; ++r) ag0[r] = au0[r] = ag1[r] = au1[r] = 0.f;
+#pragma unroll 4
+    for (int v = lane; v < kv; v += 32) {
+      const float4 g0 = __ldg(g0p + v), u0 = __ldg(u0p + v);
+      const float4 g1 = __ldg(g1p + v), u1 = __ldg(u1p + v);
+#pragma unroll
+      for (int r = 0; r < F32_ROWS; ++r) {
+        const float4 a = xs4[(int64_t)r * kv + v];
+        ag0[r] = fmaf(g0.x, a.x, ag0[r]); ag0[r] = fmaf(g0.y, a.y, ag0[r]);
+        ag0[r] = fmaf(g0.z, a.z, ag0[r]); ag0[r] = fmaf(g0.w, a.w, ag0[r]);
+        au0[r] = fmaf(u0.x, a.x, au0[r]); au0[r] = fmaf(u0.y, a.y, au0[r]);
+        au0[r] = fmaf(u0.z, a.z, au0[r]); au0[r] = fmaf(u0.w, a.w, au0[r]);
+        ag1[r] = fmaf(g1.x, a.x, ag1[r]); ag1[r] = fmaf(g1.y, a.y, ag1[r]);
+        ag1[r] = fmaf(g1.z, a.z, ag1[r]); ag1[r] = fmaf(g1.w, a.w, ag1[r]);
+        au1[r] = fmaf(u1.x, a.x, au1[r]); au1[r] = fmaf(u1.y, a.y, au1[r]);
+        au1[r] = fmaf(u1.z, a.z, au1[r]); au1[r] = fmaf(u1.w, a.w, au1[r]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < F32_ROWS; ++r) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        ag0[r] += __shfl_xor_sync(0xffffffffu, ag0[r], o);
+        au0[r] += __shfl_xor_sync(0xffffffffu, au0[r], o);
+        ag1[r] += __shfl_xor_sync(0xffffffffu, ag1[r], o);
+        au1[r] += __shfl_xor_sync(0xffffffffu, au1[r], o);
+      }
+    }
+    if (lane < rows) {
+      // select this lane's row without dynamic register indexing
+      float g0 = 0.f, u0 = 0.f, g1 = 0.f, u1 = 0.f;
+#pragma unroll
+      for (int r = 0; r < F32_ROWS; ++r)
+        if (r == lane) { g0 = ag0[r]; u0 = au0[r]; g1 = ag1[r]; u1 = au1[r]; }
+      float* orow = out + (m0 + lane) * I;
+      orow[i] = (g0 / (1.0f + expf(-g0))) * u0;
+      if (two) orow[i + 1] = (g1 / (1.0f + expf(-g1))) * u1;
+    }
+  }
+}
+
+template <typename W>
+int launch_f32(const void* x, const void* nw, const void* gw, const void* uw, void* out,
+               int64_t M, int K, int I, float eps, cudaStream_t s) {
+  const size_t smem = (size_t)F32_ROWS * K * sizeof(float);
+  if (smem > 200 * 1024) {
+    lpc::set_error("rmsswiglu_forward (fp32): dim %d too large for the fp32 path", K);
+    return LPC_ERR_UNSUPPORTED;
+  }
+  auto kfn = swiglu_f32_kernel<W>;
+  static std::atomic<uint64_t> f32_mask{0};
+  int rcx = lpc::once_per_device_smem((const void*)kfn, 200 * 1024, f32_mask);
+  if (rcx) return rcx;
+  const float* g = (const float*)gw;
+  const float* u = uw ? (const float*)uw : g + (int64_t)I * K;
+  const int gx = std::max(1, std::min(lpc::current_device_sms(), (I + 2 * F32_WARPS - 1) / (2 * F32_WARPS)));
+  const int64_t gy = (M + F32_ROWS - 1) / F32_ROWS;
+  dim3 grid((unsigned)gx, (unsigned)gy);
+  kfn<<<grid, F32_WARPS * 32, smem, s>>>((const float*)x, (const W*)nw, g, u, (float*)out, M, K, I,
+                                         eps);
+  return lpc::check_launch("rmsswiglu_forward (fp32)");
+}
+
+template <typename T>
+int launch_tc(const void* xn, const void* gw, const void* uw, void* out, int64_t M, int K, int I,
+              int dtype, cudaStream_t s) {
+  lpc::TmaDesc ta, tg, tu;
+  int rc = lpc::make_tma_2d(&ta, xn, dtype, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, BK, BM, true);
+  if (rc) return rc;
+  int up_off = 0;
+  if (uw) {
+    if ((rc = lpc::make_tma_2d(&tg, gw, dtype, K, (uint64_t)I, (uint64_t)K * 2, BK, BNI, true))) return rc;
+    if ((rc = lpc::make_tma_2d(&tu, uw, dtype, K, (uint64_t)I, (uint64_t)K * 2, BK, BNI, true))) return rc;
+  } else {
+    if ((rc = lpc::make_tma_2d(&tg, gw, dtype, K, (uint64_t)2 * I, (uint64_t)K * 2, BK, BNI, true))) return rc;
+    tu = tg;
+    up_off = I;
+  }
+  static std::atomic<uint64_t> tc_mask{0};
+  int rcx = lpc::once_per_device_smem((const void*)swiglu_tc_kernel<T>, TC_SMEM, tc_mask);
+  if (rcx) return rcx;
+  const int num_m = (int)((M + BM - 1) / BM);
+  const int num_n = (I + BNI - 1) / BNI;
+  const uint32_t idesc =
+      lpc::idesc_f16(dtype == LPC_DTYPE_BF16 ? 1u : 0u, BM, BN, 0u, 0u);
+  swiglu_tc_kernel<T><<<(unsigned)((int64_t)num_m * num_n), 192, TC_SMEM, s>>>(
+      ta, tg, tu, (T*)out, (int)M, K, I, up_off, num_m, num_n, idesc);
+  return lpc::check_launch("rmsswiglu_forward (tcgen05)");
+}
+
+}  // namespace
+
+extern "C" int64_t lpc_rmsswiglu_workspace_bytes(int64_t tokens, int dim, int dtype) {
+  if (dtype == LPC_DTYPE_F32 || tokens <= 0 || dim <= 0) return 0;
+  return tokens * (int64_t)dim * 2;
+}
+
+extern "C" int lpc_rmsswiglu_forward(const void* x, const void* rms_weight, const void* gate_w,
+                                     const void* up_w, void* out, void* workspace,
+                                     int64_t workspace_bytes, int64_t tokens, int dim, int inter,
+                                     float eps, int dtype, int w_dtype, void* stream) {
+  using namespace lpc;
+  if (!(eps > 0.f)) {
+    set_error("rmsswiglu_forward: eps must be strictly positive.");
+    return LPC_ERR_INVALID;
+  }
+  if (tokens < 0 || dim <= 0 || inter <= 0) {
+    set_error("rmsswiglu_forward: invalid sizes (tokens=%lld dim=%d inter=%d)", (long long)tokens,
+              dim, inter);
+    return LPC_ERR_INVALID;
+  }
+  if (tokens == 0) return LPC_OK;
+  if (!x || !rms_weight || !gate_w || !out) {
+    set_error("rmsswiglu_forward: null pointer");
+    return LPC_ERR_INVALID;
+  }
+  if (!aligned16(x) || !aligned16(gate_w) || (up_w && !aligned16(up_w)) || !aligned16(out)) {
+    set_error("rmsswiglu_forward: tensors must be 16-byte aligned");
+    return LPC_ERR_INVALID;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == LPC_DTYPE_F32) {
+    if (dim % 4) {
+      set_error("rmsswiglu_forward (fp32): dim must be a multiple of 4");
+      return LPC_ERR_UNSUPPORTED;
+    }
+    switch (w_dtype) {
+      case LPC_DTYPE_F32: return launch_f32<float>(x, rms_weight, gate_w, up_w, out, tokens, dim, inter, eps, s);
+      case LPC_DTYPE_BF16: return launch_f32<__nv_bfloat16>(x, rms_weight, gate_w, up_w, out, tokens, dim, inter, eps, s);
+      case LPC_DTYPE_F16: return launch_f32<__half>(x, rms_weight, gate_w, up_w, out, tokens, dim, inter, eps, s);
+    }
+    set_error("rmsswiglu_forward: unsupported weight dtype %d", w_dtype);
+    return LPC_ERR_UNSUPPORTED;
+  }
+  if (dtype != LPC_DTYPE_BF16 && dtype != LPC_DTYPE_F16) {
+    set_error("rmsswiglu_forward: unsupported dtype %d", dtype);
+    return LPC_ERR_UNSUPPORTED;
+  }
+  if (dim % BK || inter % 16) {
+    set_error("rmsswiglu_forward: tensor-core path needs dim %% 64 == 0 and inter %% 16 == 0 "
+              "(dim=%d inter=%d)", dim, inter);
+    return LPC_ERR_UNSUPPORTED;
+  }
+  if (tokens > 0x7fffffffLL) {
+    set_error("rmsswiglu_forward: too many tokens");
+    return LPC_ERR_UNSUPPORTED;
+  }
+  const int64_t need = lpc_rmsswiglu_workspace_bytes(tokens, dim, dtype);
+  if (!workspace || workspace_bytes < need || !aligned16(workspace)) {
+    set_error("rmsswiglu_forward: workspace of %lld bytes (16-byte aligned) required, got %lld",
+              (long long)need, (long long)workspace_bytes);
+    return LPC_ERR_INVALID;
+  }
+  int rc = lpc_rmsnorm_launch(x, rms_weight, workspace, tokens, dim, eps, dtype, w_dtype, s);
+  if (rc) return rc;
+  if (dtype == LPC_DTYPE_BF16)
+    return launch_tc<__nv_bfloat16>(workspace, gate_w, up_w, out, tokens, dim, inter, dtype, s);
+  return launch_tc<__half>(workspace, gate_w, up_w, out, tokens, dim, inter, dtype, s);
+}

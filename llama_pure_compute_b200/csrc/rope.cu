@@ -1,0 +1,349 @@
+// Rotary position embedding (half-split convention) and the fused
+// RoPE + KV-append prologue of the attention block.
+//
+// Math follows `_rope_forward_pytorch` (src/llama_pure_compute/ops.py:27-42):
+//   out[d]   = x[d]*cos[d]     - x[d+h]*sin[d]
+//   out[d+h] = x[d+h]*cos[d+h] + x[d]*sin[d+h]
+// evaluated in fp32 with every product and the sum rounded separately
+// (__fmul_rn / __fadd_rn, so no FMA contraction) and rounded once to the
+// storage dtype, as src/csrc/ops/rope.cu:39-45 does.  For fp32 data this is
+// bit-identical to the PyTorch fallback; for bf16/fp16 data the products of
+// two 16-bit values are exact in fp32, so the result is the correctly rounded
+// value of the exact expression.
+//
+// Each thread owns VEC consecutive rotation pairs of one (token, head): it
+// loads the VEC lower-half and VEC upper-half elements as 16-byte vectors.
+#include "lpc_common.cuh"
+
+LPC_DECLARE_STATUS(g_rope_status)
+
+unsigned int lpc_status_rope(bool clear) {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_rope_status, sizeof(v));
+  if (clear && v) {
+    unsigned int z = 0;
+    cudaMemcpyToSymbol(g_rope_status, &z, sizeof(z));
+  }
+  return v;
+}
+
+namespace {
+
+using lpc::Num;
+
+template <typename T, int N>
+__device__ __forceinline__ void load_f(const T* __restrict__ p, float (&f)[N]) {
+  constexpr int bytes = (int)sizeof(T) * N;
+  if constexpr (bytes % 16 == 0) {
+    constexpr int per = 16 / (int)sizeof(T);
+#pragma unroll
+    for (int i = 0; i < N / per; ++i) {
+      uint4 u = __ldg(reinterpret_cast<const uint4*>(p) + i);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int j = 0; j < per; ++j) f[i * per + j] = Num<T>::to_f(e[j]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) f[i] = Num<T>::to_f(p[i]);
+  }
+}
+
+// Plain (coherent) load variant for data this kernel writes in place.
+template <typename T, int N>
+__device__ __forceinline__ void load_f_rw(const T* p, float (&f)[N]) {
+  constexpr int bytes = (int)sizeof(T) * N;
+  if constexpr (bytes % 16 == 0) {
+    constexpr int per = 16 / (int)sizeof(T);
+#pragma unroll
+    for (int i = 0; i < N / per; ++i) {
+      uint4 u = reinterpret_cast<const uint4*>(p)[i];
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int j = 0; j < per; ++j) f[i * per + j] = Num<T>::to_f(e[j]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) f[i] = Num<T>::to_f(p[i]);
+  }
+}
+
+template <typename T, int N>
+__device__ __forceinline__ void store_f(T* p, const float (&f)[N]) {
+  constexpr int bytes = (int)sizeof(T) * N;
+  if constexpr (bytes % 16 == 0) {
+    constexpr int per = 16 / (int)sizeof(T);
+#pragma unroll
+    for (int i = 0; i < N / per; ++i) {
+      uint4 u;
+      T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+      for (int j = 0; j < per; ++j) e[j] = Num<T>::from_f(f[i * per + j]);
+      reinterpret_cast<uint4*>(p)[i] = u;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) p[i] = Num<T>::from_f(f[i]);
+  }
+}
+
+template <int VEC>
+__device__ __forceinline__ void rotate(const float (&x0)[VEC], const float (&x1)[VEC],
+                                       const float (&c0)[VEC], const float (&s0)[VEC],
+                                       const float (&c1)[VEC], const float (&s1)[VEC],
+                                       float (&o0)[VEC], float (&o1)[VEC]) {
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    o0[i] = __fsub_rn(__fmul_rn(x0[i], c0[i]), __fmul_rn(x1[i], s0[i]));
+    o1[i] = __fadd_rn(__fmul_rn(x1[i], c1[i]), __fmul_rn(x0[i], s1[i]));
+  }
+}
+
+// In-place RoPE on q [T, H, D] and k [T, Hkv, D].
+template <typename T, typename TT, int VEC>
+__global__ void __launch_bounds__(256) rope_kernel(T* q, T* k, const TT* __restrict__ cosb,
+                                                   const TT* __restrict__ sinb,
+                                                   const int64_t* __restrict__ pos_ids,
+                                                   int64_t num_tokens, int num_heads,
+                                                   int num_kv_heads, int head_dim, int table_mode,
+                                                   int64_t table_rows) {
+  const int half = head_dim >> 1;
+  const int chunks = half / VEC;
+  const int heads_all = num_heads + num_kv_heads;
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t work = num_tokens * heads_all * chunks;
+  if (gid >= work) return;
+  const int c = (int)(gid % chunks);
+  const int64_t th = gid / chunks;
+  const int hh = (int)(th % heads_all);
+  const int64_t t = th / heads_all;
+
+  T* row = hh < num_heads ? q + (t * num_heads + hh) * (int64_t)head_dim
+                          : k + (t * num_kv_heads + (hh - num_heads)) * (int64_t)head_dim;
+  const int d = c * VEC;
+
+  float c0[VEC], s0[VEC], c1[VEC], s1[VEC];
+  if (table_mode == 0) {
+    const int64_t r = pos_ids ? __ldg(pos_ids + t) : t;
+    if (r < 0 || r >= table_rows) {
+      atomicOr(&g_rope_status, LPC_DEV_ERR_BOUNDS);
+      return;
+    }
+    load_f<TT, VEC>(cosb + r * half + d, c0);
+    load_f<TT, VEC>(sinb + r * half + d, s0);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) { c1[i] = c0[i]; s1[i] = s0[i]; }
+  } else {
+    const TT* cr = cosb + t * (int64_t)head_dim;
+    const TT* sr = sinb + t * (int64_t)head_dim;
+    load_f<TT, VEC>(cr + d, c0);
+    load_f<TT, VEC>(sr + d, s0);
+    load_f<TT, VEC>(cr + d + half, c1);
+    load_f<TT, VEC>(sr + d + half, s1);
+  }
+  float x0[VEC], x1[VEC], o0[VEC], o1[VEC];
+  load_f_rw<T, VEC>(row + d, x0);
+  load_f_rw<T, VEC>(row + d + half, x1);
+  rotate<VEC>(x0, x1, c0, s0, c1, s1, o0, o1);
+  store_f<T, VEC>(row + d, o0);
+  store_f<T, VEC>(row + d + half, o1);
+}
+
+// Fused prologue: qkv [B, S, (H + 2Hkv) * D] -> q_out [B, H, S, D] (rotated),
+// key_cache[b, h, pos] (rotated), value_cache[b, h, pos] (copied).
+template <typename T, typename TT, int VEC>
+__global__ void __launch_bounds__(256) rope_kv_append_kernel(
+    const T* __restrict__ qkv, const int64_t* __restrict__ positions, const TT* __restrict__ cosb,
+    const TT* __restrict__ sinb, int64_t table_rows, T* __restrict__ q_out,
+    T* __restrict__ kcache, T* __restrict__ vcache, int64_t batch, int64_t seq, int num_heads,
+    int num_kv_heads, int head_dim, int64_t max_batch, int64_t max_seq_len) {
+  const int half = head_dim >> 1;
+  const int chunks = half / VEC;
+  const int heads_all = num_heads + 2 * num_kv_heads;
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t work = batch * seq * heads_all * chunks;
+  if (gid >= work) return;
+  const int c = (int)(gid % chunks);
+  const int64_t th = gid / chunks;
+  const int hh = (int)(th % heads_all);
+  const int64_t tok = th / heads_all;  // b * seq + s
+  const int64_t b = tok / seq;
+  const int64_t s = tok - b * seq;
+  const int64_t pos = __ldg(positions + tok);
+  if (pos < 0) return;
+  if (pos >= max_seq_len || pos >= table_rows || b >= max_batch) {
+    atomicOr(&g_rope_status, LPC_DEV_ERR_BOUNDS);
+    return;
+  }
+  const int d = c * VEC;
+  const T* src = qkv + tok * (int64_t)heads_all * head_dim + (int64_t)hh * head_dim;
+  float x0[VEC], x1[VEC];
+  load_f<T, VEC>(src + d, x0);
+  load_f<T, VEC>(src + d + half, x1);
+
+  if (hh >= num_heads + num_kv_heads) {  // V: plain copy into the cache
+    const int h = hh - num_heads - num_kv_heads;
+    T* dst = vcache + ((b * num_kv_heads + h) * max_seq_len + pos) * (int64_t)head_dim;
+    store_f<T, VEC>(dst + d, x0);
+    store_f<T, VEC>(dst + d + half, x1);
+    return;
+  }
+  float c0[VEC], s0[VEC], c1[VEC], s1[VEC];
+  const TT* cr = cosb + pos * (int64_t)head_dim;
+  const TT* sr = sinb + pos * (int64_t)head_dim;
+  load_f<TT, VEC>(cr + d, c0);
+  load_f<TT, VEC>(sr + d, s0);
+  load_f<TT, VEC>(cr + d + half, c1);
+  load_f<TT, VEC>(sr + d + half, s1);
+  float o0[VEC], o1[VEC];
+  rotate<VEC>(x0, x1, c0, s0, c1, s1, o0, o1);
+  T* dst;
+  if (hh < num_heads) {
+    dst = q_out + ((b * num_heads + hh) * seq + s) * (int64_t)head_dim;
+  } else {
+    const int h = hh - num_heads;
+    dst = kcache + ((b * num_kv_heads + h) * max_seq_len + pos) * (int64_t)head_dim;
+  }
+  store_f<T, VEC>(dst + d, o0);
+  store_f<T, VEC>(dst + d + half, o1);
+}
+
+template <typename T, typename TT>
+int launch_rope(void* q, void* k, const void* cosb, const void* sinb, const int64_t* pos,
+                int64_t num_tokens, int num_heads, int num_kv_heads, int head_dim, int table_mode,
+                int64_t table_rows, bool vec_ok, cudaStream_t s) {
+  constexpr int VEC = 16 / (int)sizeof(T);
+  const int heads_all = num_heads + num_kv_heads;
+  const int threads = 256;
+  if (vec_ok) {
+    const int64_t work = num_tokens * heads_all * (head_dim / 2 / VEC);
+    rope_kernel<T, TT, VEC><<<(unsigned)((work + threads - 1) / threads), threads, 0, s>>>(
+        (T*)q, (T*)k, (const TT*)cosb, (const TT*)sinb, pos, num_tokens, num_heads, num_kv_heads,
+        head_dim, table_mode, table_rows);
+  } else {
+    const int64_t work = num_tokens * heads_all * (head_dim / 2);
+    rope_kernel<T, TT, 1><<<(unsigned)((work + threads - 1) / threads), threads, 0, s>>>(
+        (T*)q, (T*)k, (const TT*)cosb, (const TT*)sinb, pos, num_tokens, num_heads, num_kv_heads,
+        head_dim, table_mode, table_rows);
+  }
+  return lpc::check_launch("rope_forward");
+}
+
+template <typename T>
+int launch_rope_t(int table_dtype, void* q, void* k, const void* c, const void* sn,
+                  const int64_t* pos, int64_t n, int h, int hkv, int d, int mode, int64_t rows,
+                  bool vec_ok, cudaStream_t s) {
+  switch (table_dtype) {
+    case LPC_DTYPE_F32: return launch_rope<T, float>(q, k, c, sn, pos, n, h, hkv, d, mode, rows, vec_ok, s);
+    case LPC_DTYPE_BF16: return launch_rope<T, __nv_bfloat16>(q, k, c, sn, pos, n, h, hkv, d, mode, rows, vec_ok, s);
+    case LPC_DTYPE_F16: return launch_rope<T, __half>(q, k, c, sn, pos, n, h, hkv, d, mode, rows, vec_ok, s);
+  }
+  lpc::set_error("rope_forward: unsupported table dtype %d", table_dtype);
+  return LPC_ERR_UNSUPPORTED;
+}
+
+template <typename T, typename TT>
+int launch_fused(const void* qkv, const int64_t* positions, const void* c, const void* sn,
+                 int64_t rows, void* q_out, void* kc, void* vc, int64_t batch, int64_t seq, int h,
+                 int hkv, int d, int64_t max_batch, int64_t max_seq, cudaStream_t s) {
+  constexpr int VEC = 16 / (int)sizeof(T);
+  const int threads = 256;
+  const int64_t work = batch * seq * (h + 2 * hkv) * (d / 2 / VEC);
+  rope_kv_append_kernel<T, TT, VEC><<<(unsigned)((work + threads - 1) / threads), threads, 0, s>>>(
+      (const T*)qkv, positions, (const TT*)c, (const TT*)sn, rows, (T*)q_out, (T*)kc, (T*)vc, batch,
+      seq, h, hkv, d, max_batch, max_seq);
+  return lpc::check_launch("rope_kv_append");
+}
+
+}  // namespace
+
+extern "C" int lpc_rope_forward(void* q, void* k, const void* cos, const void* sin,
+                                const int64_t* position_ids, int64_t num_tokens, int num_heads,
+                                int num_kv_heads, int head_dim, int table_mode, int64_t table_rows,
+                                int q_dtype, int table_dtype, void* stream) {
+  using namespace lpc;
+  if (num_tokens < 0 || num_heads <= 0 || num_kv_heads < 0 || head_dim <= 0 || head_dim % 2) {
+    set_error("rope_forward: invalid sizes (tokens=%lld heads=%d kv_heads=%d dim=%d)",
+              (long long)num_tokens, num_heads, num_kv_heads, head_dim);
+    return LPC_ERR_INVALID;
+  }
+  if (table_mode != 0 && table_mode != 1) {
+    set_error("rope_forward: table_mode must be 0 or 1");
+    return LPC_ERR_INVALID;
+  }
+  if (num_tokens == 0) return LPC_OK;
+  if (!q || !cos || !sin || (num_kv_heads > 0 && !k)) {
+    set_error("rope_forward: null pointer");
+    return LPC_ERR_INVALID;
+  }
+  const int es = dtype_size(q_dtype), ts = dtype_size(table_dtype);
+  if (!es || !ts) {
+    set_error("rope_forward: unsupported dtype (q=%d table=%d)", q_dtype, table_dtype);
+    return LPC_ERR_UNSUPPORTED;
+  }
+  const int vec = 16 / es;
+  const int half = head_dim / 2;
+  const int64_t table_row_elems = table_mode == 0 ? half : head_dim;
+  bool vec_ok = (half % vec == 0) && aligned16(q) && (num_kv_heads == 0 || aligned16(k)) &&
+                aligned16(cos) && aligned16(sin) && ((int64_t)head_dim * es) % 16 == 0 &&
+                (table_row_elems * ts) % 16 == 0 && ((int64_t)vec * ts) % 16 == 0 &&
+                ((int64_t)half * ts) % 16 == 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (q_dtype) {
+    case LPC_DTYPE_F32: return launch_rope_t<float>(table_dtype, q, k, cos, sin, position_ids, num_tokens, num_heads, num_kv_heads, head_dim, table_mode, table_rows, vec_ok, s);
+    case LPC_DTYPE_BF16: return launch_rope_t<__nv_bfloat16>(table_dtype, q, k, cos, sin, position_ids, num_tokens, num_heads, num_kv_heads, head_dim, table_mode, table_rows, vec_ok, s);
+    case LPC_DTYPE_F16: return launch_rope_t<__half>(table_dtype, q, k, cos, sin, position_ids, num_tokens, num_heads, num_kv_heads, head_dim, table_mode, table_rows, vec_ok, s);
+  }
+  return LPC_ERR_UNSUPPORTED;
+}
+
+extern "C" int lpc_rope_kv_append(const void* qkv, const int64_t* positions, const void* cos,
+                                  const void* sin, int64_t table_rows, void* q_out,
+                                  void* key_cache, void* value_cache, int64_t batch, int64_t seq,
+                                  int num_heads, int num_kv_heads, int head_dim,
+                                  int64_t max_batch, int64_t max_seq_len, int dtype,
+                                  int table_dtype, void* stream) {
+  using namespace lpc;
+  if (batch < 0 || seq < 0 || num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 ||
+      max_batch <= 0 || max_seq_len <= 0 || table_rows <= 0) {
+    set_error("rope_kv_append: invalid sizes");
+    return LPC_ERR_INVALID;
+  }
+  if (batch == 0 || seq == 0) return LPC_OK;
+  if (batch > max_batch) {
+    set_error("rope_kv_append: batch %lld exceeds cache capacity %lld", (long long)batch,
+              (long long)max_batch);
+    return LPC_ERR_INVALID;
+  }
+  if (!qkv || !positions || !cos || !sin || !q_out || !key_cache || !value_cache) {
+    set_error("rope_kv_append: null pointer");
+    return LPC_ERR_INVALID;
+  }
+  const int es = dtype_size(dtype), ts = dtype_size(table_dtype);
+  if (dtype == LPC_DTYPE_F32 || !es || !ts) {
+    set_error("rope_kv_append: needs bf16/fp16 activations (got dtype %d, table %d)", dtype,
+              table_dtype);
+    return LPC_ERR_UNSUPPORTED;
+  }
+  const int vec = 16 / es;
+  if ((head_dim / 2) % vec || !aligned16(qkv) || !aligned16(q_out) || !aligned16(key_cache) ||
+      !aligned16(value_cache) || !aligned16(cos) || !aligned16(sin) ||
+      ((int64_t)head_dim * ts) % 16 || ((int64_t)vec * ts) % 16) {
+    set_error("rope_kv_append: head_dim/alignment not supported by the 16-byte vector path");
+    return LPC_ERR_UNSUPPORTED;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == LPC_DTYPE_BF16) {
+    if (table_dtype == LPC_DTYPE_BF16)
+      return launch_fused<__nv_bfloat16, __nv_bfloat16>(qkv, positions, cos, sin, table_rows, q_out, key_cache, value_cache, batch, seq, num_heads, num_kv_heads, head_dim, max_batch, max_seq_len, s);
+    if (table_dtype == LPC_DTYPE_F32)
+      return launch_fused<__nv_bfloat16, float>(qkv, positions, cos, sin, table_rows, q_out, key_cache, value_cache, batch, seq, num_heads, num_kv_heads, head_dim, max_batch, max_seq_len, s);
+  } else {
+    if (table_dtype == LPC_DTYPE_F16)
+      return launch_fused<__half, __half>(qkv, positions, cos, sin, table_rows, q_out, key_cache, value_cache, batch, seq, num_heads, num_kv_heads, head_dim, max_batch, max_seq_len, s);
+    if (table_dtype == LPC_DTYPE_F32)
+      return launch_fused<__half, float>(qkv, positions, cos, sin, table_rows, q_out, key_cache, value_cache, batch, seq, num_heads, num_kv_heads, head_dim, max_batch, max_seq_len, s);
+  }
+  set_error("rope_kv_append: table dtype must match activations or be fp32");
+  return LPC_ERR_UNSUPPORTED;
+}

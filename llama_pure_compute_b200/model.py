@@ -1,0 +1,340 @@
+"""Llama model graph on the sm_100a hot-path kernels.
+
+Class names, constructor arguments, parameter names (state-dict keys) and
+forward signatures follow src/llama_pure_compute/model.py:28-580, so
+checkpoints and call sites carry over.  What runs underneath:
+
+  input_layernorm   -> lpc_rmsnorm_forward (model.py:305 via rmsnorm.py)
+  q/k/v projections -> one GEMM on the concatenated [(H+2Hkv)*D, dim] weight
+                       (cuBLAS through torch; the q/k/v parameters are views of it)
+  RoPE + KV append  -> lpc_rope_kv_append (model.py:146-168 fused into one kernel;
+                       per-row positions, so batches may be ragged)
+  attention         -> decode: lpc_decode_attention over device seq_lens
+                       (no per-layer .item() sync, model.py:159-161);
+                       prefill / no cache: lpc_flash_attention (tcgen05)
+  o_proj + residual -> one addmm (residual added in the GEMM epilogue)
+  post norm + SwiGLU-> lpc_rmsswiglu_forward (model.py:315-321; tcgen05 GEMM
+                       with the SiLU*up epilogue, no torch.cat of weights)
+  down + residual   -> one addmm
+  lm_head           -> all positions by default (model.py:475), or only the
+                       last one with ``last_token_only=True``
+
+There is no PyTorch attention fallback: a custom additive ``mask`` raises.
+"""
+from __future__ import annotations
+
+import math
+import os
+from typing import Dict, Optional, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .config import LlamaModelConfig
+from .flash_attention import flash_attention_v2
+from .kv_manager import KVCacheManager
+from .ops import decode_attention, rmsswiglu_forward, rope_forward
+from .rmsnorm import RMSNorm
+
+__all__ = ["precompute_freqs_cis", "LlamaAttention", "LlamaDecodeLayer", "LlamaModel",
+           "LlamaForCausalLM"]
+
+
+def precompute_freqs_cis(dim: int, end: int, theta: float = 10000.0,
+                         device: Optional[torch.device] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin tables [end, dim], halves duplicated (model.py:28-64)."""
+    inv = 1.0 / (theta ** (torch.arange(0, dim, 2, device=device, dtype=torch.float32) / dim))
+    t = torch.arange(end, device=device, dtype=torch.float32)
+    f = torch.outer(t, inv)
+    f = torch.cat([f, f], dim=-1)
+    return torch.cos(f), torch.sin(f)
+
+
+class _StepContext:
+    """Per-forward data shared by all layers (computed once, not per layer)."""
+
+    __slots__ = ("positions", "seq_lens", "start_pos", "cos_table", "sin_table", "decode",
+                 "workspace")
+
+    def __init__(self):
+        self.positions = None
+        self.seq_lens = None
+        self.start_pos = None
+        self.cos_table = None
+        self.sin_table = None
+        self.decode = False
+        self.workspace = None
+
+
+class LlamaAttention(nn.Module):
+    def __init__(self, config: LlamaModelConfig) -> None:
+        super().__init__()
+        self.config = config
+        self.dim = config.dim
+        self.num_heads = config.num_heads
+        self.num_kv_heads = config.num_kv_heads
+        self.head_dim = config.head_dim
+        self.num_kv_groups = config.gqa_group_size
+        self.scale = self.head_dim ** -0.5
+        self.q_proj = nn.Linear(self.dim, self.num_heads * self.head_dim, bias=False)
+        self.k_proj = nn.Linear(self.dim, self.num_kv_heads * self.head_dim, bias=False)
+        self.v_proj = nn.Linear(self.dim, self.num_kv_heads * self.head_dim, bias=False)
+        self.o_proj = nn.Linear(self.num_heads * self.head_dim, self.dim, bias=False)
+        self._qkv_key = None
+        self._qkv = None
+
+    def qkv_weight(self) -> torch.Tensor:
+        """[(H+2Hkv)*D, dim] weight; q/k/v parameters are re-pointed into it once."""
+        ws = (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
+        key = tuple((w.data_ptr(), w._version, w.dtype, w.device) for w in ws)
+        if self._qkv is None or key != self._qkv_key:
+            fused = torch.cat([w.detach() for w in ws], dim=0).contiguous()
+            n_q = self.num_heads * self.head_dim
+            n_kv = self.num_kv_heads * self.head_dim
+            with torch.no_grad():
+                self.q_proj.weight.data = fused[:n_q]
+                self.k_proj.weight.data = fused[n_q:n_q + n_kv]
+                self.v_proj.weight.data = fused[n_q + n_kv:]
+            self._qkv = fused
+            ws = (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
+            self._qkv_key = tuple((w.data_ptr(), w._version, w.dtype, w.device) for w in ws)
+        return self._qkv
+
+    def forward(
+        self,
+        x: torch.Tensor,
+        *,
+        positions: torch.Tensor,
+        cos: torch.Tensor,
+        sin: torch.Tensor,
+        kv_cache: Optional[KVCacheManager],
+        layer_idx: int,
+        mask: Optional[torch.Tensor] = None,
+        use_triton_flash: bool = True,
+        ctx: Optional[_StepContext] = None,
+    ) -> torch.Tensor:
+        """Attention block output before the residual add (model.py:110-249)."""
+        if mask is not None:
+            raise NotImplementedError(
+                "custom attention masks are not supported by the B200 kernels; causal attention "
+                "is applied by passing mask=None")
+        B, S, _ = x.shape
+        H, Hkv, D = self.num_heads, self.num_kv_heads, self.head_dim
+        qkv = F.linear(x, self.qkv_weight())
+        if kv_cache is not None:
+            if ctx is None or ctx.cos_table is None:
+                raise ValueError("cached attention needs the model's RoPE tables (call via LlamaModel)")
+            q = kv_cache.append_qkv(layer_idx=layer_idx, qkv=qkv, positions=positions,
+                                    cos_table=ctx.cos_table, sin_table=ctx.sin_table, num_heads=H)
+            kc, vc = kv_cache.k_cache[layer_idx], kv_cache.v_cache[layer_idx]
+            if ctx.decode:
+                out = decode_attention(q.view(B, H, D), kc, vc, ctx.seq_lens, self.scale,
+                                       workspace=ctx.workspace)
+                out = out.view(B, 1, H * D)
+            else:
+                end = ctx.start_pos + S
+                out = flash_attention_v2(q, kc[:B, :, :end, :], vc[:B, :, :end, :], causal=True,
+                                         sm_scale=self.scale)
+                out = out.transpose(1, 2).reshape(B, S, H * D)
+        else:
+            q = qkv[..., : H * D].reshape(B, S, H, D)
+            k = qkv[..., H * D:(H + Hkv) * D].reshape(B, S, Hkv, D)
+            v = qkv[..., (H + Hkv) * D:].reshape(B, S, Hkv, D)
+            q, k = rope_forward(q, k, cos, sin, positions)
+            out = flash_attention_v2(q.transpose(1, 2).contiguous(), k.transpose(1, 2).contiguous(),
+                                     v.transpose(1, 2).contiguous(), causal=True,
+                                     sm_scale=self.scale)
+            out = out.transpose(1, 2).reshape(B, S, H * D)
+        return out
+
+    def project_out(self, attn: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+        """residual + attn @ o_proj^T in one GEMM (beta=1 epilogue)."""
+        shp = residual.shape
+        r2 = residual.reshape(-1, shp[-1])
+        return torch.addmm(r2, attn.reshape(-1, attn.shape[-1]), self.o_proj.weight.t()).view(shp)
+
+
+class LlamaDecodeLayer(nn.Module):
+    def __init__(self, config: LlamaModelConfig, layer_idx: int) -> None:
+        super().__init__()
+        self.layer_idx = layer_idx
+        self.input_layernorm = RMSNorm(config.dim, eps=config.rms_norm_eps)
+        self.self_attn = LlamaAttention(config)
+        self.post_attention_layernorm = RMSNorm(config.dim, eps=config.rms_norm_eps)
+        self.gate_proj = nn.Linear(config.dim, config.inter_dim, bias=False)
+        self.up_proj = nn.Linear(config.dim, config.inter_dim, bias=False)
+        self.down_proj = nn.Linear(config.inter_dim, config.dim, bias=False)
+
+    def forward(
+        self,
+        x: torch.Tensor,
+        *,
+        positions: torch.Tensor,
+        cos: torch.Tensor,
+        sin: torch.Tensor,
+        kv_cache: Optional[KVCacheManager],
+        mask: Optional[torch.Tensor],
+        ctx: Optional[_StepContext] = None,
+    ) -> torch.Tensor:
+        attn = self.self_attn(self.input_layernorm(x), positions=positions, cos=cos, sin=sin,
+                              kv_cache=kv_cache, layer_idx=self.layer_idx, mask=mask, ctx=ctx)
+        h = self.self_attn.project_out(attn, x)
+        mlp_inter = rmsswiglu_forward(h, rms_weight=self.post_attention_layernorm.weight,
+                                      gate_w=self.gate_proj.weight, up_w=self.up_proj.weight,
+                                      eps=self.post_attention_layernorm.eps)
+        shp = h.shape
+        return torch.addmm(h.reshape(-1, shp[-1]), mlp_inter.reshape(-1, mlp_inter.shape[-1]),
+                           self.down_proj.weight.t()).view(shp)
+
+
+class LlamaModel(nn.Module):
+    def __init__(self, config: LlamaModelConfig) -> None:
+        super().__init__()
+        self.config = config
+        self.embed_tokens = nn.Embedding(config.vocab_size, config.dim)
+        self.layers = nn.ModuleList([LlamaDecodeLayer(config, i) for i in range(config.num_layers)])
+        self.norm = RMSNorm(config.dim, eps=config.rms_norm_eps)
+        cos, sin = precompute_freqs_cis(config.head_dim, config.max_seq_len, theta=config.rope_theta)
+        self.register_buffer("cos_cached", cos, persistent=False)
+        self.register_buffer("sin_cached", sin, persistent=False)
+        self._decode_ws: Dict[tuple, torch.Tensor] = {}
+
+    def reset_rope_tables(self) -> None:
+        """Recompute cos/sin (e.g. after materialising a meta-device model)."""
+        dev = self.embed_tokens.weight.device
+        cos, sin = precompute_freqs_cis(self.config.head_dim, self.config.max_seq_len,
+                                        theta=self.config.rope_theta, device=dev)
+        dt = self.embed_tokens.weight.dtype
+        self.cos_cached = cos.to(dt)
+        self.sin_cached = sin.to(dt)
+
+    def _workspace(self, batch: int, max_seq_len: int, device) -> torch.Tensor:
+        from .ops import decode_attention_workspace
+        key = (batch, max_seq_len, str(device))
+        ws = self._decode_ws.get(key)
+        if ws is None:
+            ws = decode_attention_workspace(batch, self.config.num_heads, max_seq_len,
+                                            self.config.head_dim, device)
+            self._decode_ws = {key: ws}
+        return ws
+
+    def forward(
+        self,
+        input_ids: torch.Tensor,
+        *,
+        positions: torch.Tensor,
+        kv_cache: Optional[KVCacheManager],
+        mask: Optional[torch.Tensor],
+    ) -> torch.Tensor:
+        h = self.embed_tokens(input_ids)
+        B, S = input_ids.shape
+        ctx = _StepContext()
+        ctx.positions = positions
+        cos = sin = None
+        if kv_cache is not None:
+            ctx.cos_table, ctx.sin_table = self.cos_cached, self.sin_cached
+            if S == 1:
+                ctx.decode = True
+                ctx.seq_lens = kv_cache.set_seq_lens(positions)
+                ctx.workspace = self._workspace(B, kv_cache.max_seq_len, h.device)
+            else:
+                # one host read per forward (the reference reads it in every layer)
+                ctx.start_pos = int(positions[0, 0].item())
+                kv_cache.seq_lens[:B] = ctx.start_pos + S
+        else:
+            cos = self.cos_cached[positions]
+            sin = self.sin_cached[positions]
+            if cos.ndim == 3:
+                cos = cos.unsqueeze(2)
+                sin = sin.unsqueeze(2)
+        for layer in self.layers:
+            h = layer(h, positions=positions, cos=cos, sin=sin, kv_cache=kv_cache, mask=mask,
+                      ctx=ctx)
+        return self.norm(h)
+
+
+class LlamaForCausalLM(nn.Module):
+    def __init__(self, config: LlamaModelConfig) -> None:
+        super().__init__()
+        self.config = config
+        self.model = LlamaModel(config)
+        self.lm_head = nn.Linear(config.dim, config.vocab_size, bias=False)
+
+    def forward(
+        self,
+        input_ids: torch.Tensor,
+        *,
+        positions: Optional[torch.Tensor] = None,
+        kv_cache: Optional[KVCacheManager] = None,
+        mask: Optional[torch.Tensor] = None,
+        last_token_only: bool = False,
+    ) -> torch.Tensor:
+        """Logits [B, S, vocab] (model.py:427-477); [B, 1, vocab] with
+        ``last_token_only``.  Without a cache the causal mask is applied by the
+        attention kernel itself (the reference builds a -inf triu mask, model.py:451-466)."""
+        B, S = input_ids.shape
+        if positions is None:
+            positions = torch.arange(S, device=input_ids.device).unsqueeze(0).expand(B, -1)
+        hidden = self.model(input_ids, positions=positions, kv_cache=kv_cache, mask=mask)
+        if last_token_only:
+            hidden = hidden[:, -1:, :]
+        return self.lm_head(hidden)
+
+    # -- construction helpers ----------------------------------------------
+    @classmethod
+    def random_init(cls, config: LlamaModelConfig, *, device="cuda", dtype=torch.bfloat16,
+                    seed: int = 0, std: float = 0.02) -> "LlamaForCausalLM":
+        """Random-init model built directly in device memory: every matrix
+        ~N(0, std) drawn from a generator seeded with ``seed`` on ``device``,
+        RMSNorm weights 1.0."""
+        with torch.device("meta"):
+            model = cls(config)
+        model = model.to_empty(device=device).to(dtype)
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed)
+        with torch.no_grad():
+            for name, p in model.named_parameters():
+                if name.endswith("layernorm.weight") or name == "model.norm.weight":
+                    p.fill_(1.0)
+                else:
+                    p.normal_(0.0, std, generator=gen)
+        model.model.reset_rope_tables()
+        model.eval()
+        return model
+
+    @classmethod
+    def from_state_dict(cls, config: LlamaModelConfig, state_dict: Dict[str, torch.Tensor], *,
+                        device="cuda", dtype=torch.bfloat16) -> "LlamaForCausalLM":
+        with torch.device("meta"):
+            model = cls(config)
+        model = model.to_empty(device=device).to(dtype)
+        missing, unexpected = model.load_state_dict(state_dict, strict=False)
+        if missing:
+            raise RuntimeError("Missing checkpoint weights:\n" + "\n".join(missing))
+        if unexpected:
+            raise RuntimeError("Unexpected checkpoint weights:\n" + "\n".join(unexpected))
+        model.model.reset_rope_tables()
+        model.eval()
+        return model
+
+    @classmethod
+    def from_pretrained(cls, model_dir: str, *, device: str = "cuda",
+                        dtype: torch.dtype = torch.float16) -> "LlamaForCausalLM":
+        """Loads config.json + .safetensors/.bin with strict key checks (model.py:479-580)."""
+        cfg_file = os.path.join(model_dir, "config.json")
+        if not os.path.isfile(cfg_file):
+            raise FileNotFoundError(f"Missing config: {cfg_file}")
+        config = LlamaModelConfig.from_json(cfg_file)
+        files = [os.path.join(model_dir, f) for f in os.listdir(model_dir)
+                 if f.endswith((".safetensors", ".bin"))]
+        if not files:
+            raise FileNotFoundError(f"No checkpoint weights found in {model_dir}")
+        sd: Dict[str, torch.Tensor] = {}
+        for f in files:
+            if f.endswith(".safetensors"):
+                from safetensors.torch import load_file
+                sd.update(load_file(f, device="cpu"))
+            else:
+                sd.update(torch.load(f, map_location="cpu", weights_only=True))
+        return cls.from_state_dict(config, sd, device=device, dtype=dtype)

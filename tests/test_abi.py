@@ -1,0 +1,92 @@
+"""C-ABI library: builds, loads without a GPU, exports every declared symbol,
+and rejects bad arguments on the host (no kernel is launched in these tests)."""
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from llama_pure_compute_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "lpc_b200.h"
+
+
+def declared():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"LPC_API\s+[\w\s\*]+?\b(lpc_\w+)\s*\(", text)))
+
+
+def test_header_declares_all_bound_symbols():
+    assert set(declared()) == set(_lib.exported_symbols())
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True,
+                         text=True).stdout
+    exported = set(re.findall(r"\bT (lpc_\w+)", out))
+    for name in declared():
+        assert name in exported, name
+        assert getattr(lib, name) is not None
+
+
+def test_version_and_error_string():
+    lib = _lib.load()
+    assert lib.lpc_version() >= 100
+    assert isinstance(lib.lpc_last_error(), bytes)
+
+
+def test_host_validation_without_gpu():
+    lib = _lib.load()
+    # negative sizes / bad eps are rejected before any CUDA call
+    assert lib.lpc_rmsnorm_forward(None, None, None, -1, 16, 1e-5, 2, 2, None) == _lib.LPC_ERR_INVALID
+    assert b"invalid sizes" in lib.lpc_last_error()
+    assert lib.lpc_rmsnorm_forward(None, None, None, 4, 16, 0.0, 2, 2, None) == _lib.LPC_ERR_INVALID
+    assert lib.lpc_rmsswiglu_forward(None, None, None, None, None, None, 0, 4, 64, 64, -1.0, 2, 2,
+                                     None) == _lib.LPC_ERR_INVALID
+    assert b"eps must be strictly positive" in lib.lpc_last_error()
+    assert lib.lpc_update_kv_cache(None, None, None, None, None, 4, 64, 1, 64, 1, 8, 3,
+                                   None) == _lib.LPC_ERR_UNSUPPORTED
+    assert lib.lpc_flash_attention(None, None, None, None, 1, 2, 2, 8, 4, 128, 0, 0, 1, 1.0, 2,
+                                   None) == _lib.LPC_ERR_INVALID
+    assert b"Q_LEN cannot exceed KV_LEN" in lib.lpc_last_error()
+    assert lib.lpc_decode_attention(None, None, None, None, None, None, 0, 2, 3, 2, 128, 4, 64, 1.0,
+                                    2, None) == _lib.LPC_ERR_INVALID
+    # zero-sized work is a no-op
+    assert lib.lpc_update_kv_cache(None, None, None, None, None, 0, 64, 1, 64, 1, 8, 2, None) == 0
+
+
+def test_workspace_queries():
+    lib = _lib.load()
+    assert lib.lpc_rmsswiglu_workspace_bytes(256, 4096, 2) == 256 * 4096 * 2
+    assert lib.lpc_rmsswiglu_workspace_bytes(8, 4096, 0) == 0
+    n = lib.lpc_decode_attention_workspace_bytes(64, 32, 4097, 128)
+    assert n == 64 * 32 * 17 * 130 * 4
+
+
+def test_error_translation():
+    lib = _lib.load()
+    lib.lpc_rmsnorm_forward(None, None, None, -1, 16, 1e-5, 2, 2, None)
+    with pytest.raises(ValueError):
+        _lib.check(_lib.LPC_ERR_INVALID, "x")
+    with pytest.raises(TypeError):
+        _lib.check(_lib.LPC_ERR_UNSUPPORTED, "x")
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.LPC_ERR_CUDA, "x")
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    with pytest.raises(_lib.BackendUnavailable):
+        _lib.load(tmp_path / "nope.so")
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+    from llama_pure_compute_b200 import ops
+    q = torch.zeros(1, 2, 128)
+    with pytest.raises(ValueError, match="must be on CUDA device"):
+        ops.rope_forward(q, q, torch.zeros(4, 64), torch.zeros(4, 64))
+    with pytest.raises(ValueError):
+        ops.rmsswiglu_forward(torch.zeros(2, 64), torch.ones(64), torch.zeros(64, 64),
+                              torch.zeros(64, 64))
