@@ -60,6 +60,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=32, help="(debug only) fewer layers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--suite", choices=["decode", "ops"], default="decode",
+                    help="decode: the 7B decode workload (default); ops: per-op roofline lines")
+    ap.add_argument("--only", default="", help="comma list of op lines for --suite ops")
     return ap.parse_args()
 
 
@@ -139,11 +142,17 @@ def shard(global_batch: int, world: int, rank: int):
     return start, per + (1 if rank < extra else 0)
 
 
+def _coll_device():
+    import torch.distributed as dist
+    return "cpu" if dist.get_backend() == "gloo" else "cuda"
+
+
 def max_over_ranks(x: float, world: int) -> float:
+    """Max of a per-rank scalar (timings are reported as the slowest rank)."""
     if world == 1:
         return x
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    t = torch.tensor([x], dtype=torch.float64, device=_coll_device())
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -151,9 +160,10 @@ def max_over_ranks(x: float, world: int) -> float:
 def barrier(world: int):
     if world > 1:
         import torch.distributed as dist
-        t = torch.zeros(1, device="cuda")
+        t = torch.zeros(1, device=_coll_device())
         dist.all_reduce(t)
-    torch.cuda.synchronize()
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
 
 
 def model_config(layers: int, max_seq: int):
@@ -431,8 +441,135 @@ def run_ours(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# per-op roofline lines (--suite ops)
+# ---------------------------------------------------------------------------
+def _peaks():
+    try:
+        return json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        return {}
+
+
+def _time_us(fn, reps: int, flush=None, warm: int = 3) -> float:
+    """Mean device time of fn() in microseconds: CUDA events on the current
+    stream, `flush` (an L2-sized write) between launches when given; the
+    flush is timed separately and subtracted."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    total = 0.0
+    for _ in range(reps):
+        if flush is not None:
+            flush()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        fn()
+        b.record(st)
+        b.synchronize()
+        total += a.elapsed_time(b)
+    return total / reps * 1e3
+
+
+def run_ops(args):
+    from llama_pure_compute_b200 import ops
+    from llama_pure_compute_b200.flash_attention import flash_attention_v2
+    from llama_pure_compute_b200.model import precompute_freqs_cis
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pk = _peaks()
+    hbm = pk.get("hbm_gbs", 6650.0)
+    tc = pk.get("bf16_tflops", 1590.0)
+    src = "MEASURED_PEAKS.json" if pk else "fallback"
+    scratch = torch.empty(256 * 2**20, dtype=torch.uint8, device=dev)  # > L2 (126 MB)
+    flush = lambda: scratch.fill_(1)  # noqa: E731
+    only = set(filter(None, args.only.split(",")))
+    out = []
+
+    def emit(d):
+        d.setdefault("peak_source", src)
+        out.append(d)
+        print(json.dumps(d), flush=True)
+
+    if not only or "rmsswiglu_f32" in only:
+        torch.manual_seed(0)
+        x = torch.randn(8, 4096, device=dev)
+        w = 1 + 0.02 * torch.randn(4096, device=dev)
+        gw = 0.02 * torch.randn(11008, 4096, device=dev)
+        uw = 0.02 * torch.randn(11008, 4096, device=dev)
+        us = _time_us(lambda: ops.rmsswiglu_forward(x, w, gw, uw, 1e-6), 20, flush)
+        byt = (2 * 11008 * 4096 + 8 * 4096 + 4096 + 8 * 11008) * 4
+        emit({"op": "rmsswiglu_fp32 x[8,4096] W 2x[11008,4096]", "kernel": "swiglu_f32_kernel",
+              "us": round(us, 2), "bytes": byt, "achieved_gbs": round(byt / us / 1e3, 1),
+              "peak_gbs": hbm, "frac": round(byt / us / 1e3 / hbm, 4), "bound": "hbm",
+              "l2": "flushed between launches"})
+        del gw, uw
+    if not only or "rmsswiglu_bf16" in only:
+        for M in (256, 128, 64, 32):
+            g = torch.Generator(device=dev).manual_seed(M)
+            x = torch.randn(M, 4096, device=dev, generator=g).to(torch.bfloat16)
+            w = torch.ones(4096, device=dev, dtype=torch.bfloat16)
+            gw = (0.02 * torch.randn(11008, 4096, device=dev, generator=g)).to(torch.bfloat16)
+            uw = (0.02 * torch.randn(11008, 4096, device=dev, generator=g)).to(torch.bfloat16)
+            us = _time_us(lambda: ops.rmsswiglu_forward(x, w, gw, uw, 1e-5), 20, flush)
+            byt = (2 * 11008 * 4096 + M * 4096 * 2 + M * 11008) * 2
+            fl = 2 * M * 4096 * 2 * 11008
+            emit({"op": f"rmsswiglu_bf16 7B layer M={M}", "kernel": "rmsnorm_vec + swiglu_tc_kernel",
+                  "us": round(us, 2), "bytes": byt, "achieved_gbs": round(byt / us / 1e3, 1),
+                  "frac_hbm": round(byt / us / 1e3 / hbm, 4), "tflops": round(fl / us / 1e6, 1),
+                  "frac_tc": round(fl / us / 1e6 / tc, 4), "l2": "flushed between launches"})
+    if not only or "prefill" in only:
+        torch.manual_seed(1)
+        q, k, v = (torch.randn(4, 32, 2048, 128, device=dev).to(torch.bfloat16) for _ in range(3))
+        us = _time_us(lambda: flash_attention_v2(q, k, v, causal=True,
+                                                 sm_scale=1 / math.sqrt(128)), 20)
+        fl = 2 * 4 * 32 * 2048 * 2048 * 128
+        emit({"op": "prefill attention [4,32,2048,128] causal bf16", "kernel": "flash_prefill_kernel",
+              "us": round(us, 2), "flops": fl, "tflops": round(fl / us / 1e6, 1), "peak_tflops": tc,
+              "frac": round(fl / us / 1e6 / tc, 4), "bound": "tensor",
+              "flop_model": "2*B*H*S^2*D (benchmark_attention.py:104-116)",
+              "l2": "inputs 201 MB > L2"})
+    if not only or "decode" in only:
+        torch.manual_seed(2)
+        B, H, D = 64, 32, 128
+        L = torch.randint(128, 4097, (B,))
+        Smax = 4097
+        kc = torch.randn(B, H, Smax, D, device=dev, dtype=torch.bfloat16)
+        vc = torch.randn(B, H, Smax, D, device=dev, dtype=torch.bfloat16)
+        qkv = torch.randn(B, 1, 3 * H * D, device=dev).to(torch.bfloat16)
+        cos, sin = precompute_freqs_cis(D, Smax, device=dev)
+        cos, sin = cos.to(torch.bfloat16), sin.to(torch.bfloat16)
+        pos = L.view(B, 1).to(dev)
+        lens = (L + 1).to(torch.int32).to(dev)
+        ws = ops.decode_attention_workspace(B, H, Smax, D, dev)
+        outb = torch.empty(B, H, D, device=dev, dtype=torch.bfloat16)
+
+        def step():
+            qq = ops.rope_kv_append(qkv, pos, cos, sin, kc, vc, H, H)
+            ops.decode_attention(qq.view(B, H, D), kc, vc, lens, None, outb, ws)
+
+        us = _time_us(step, 20, flush)
+        byt = int((L + 1).sum()) * H * D * 2 * 2 + 3 * B * H * D * 2 * 2
+        emit({"op": "decode step 64 ragged seqs L~U[128,4096] (rope+append+attention)",
+              "kernel": "rope_kv_append_kernel + decode_split_kernel + decode_combine_kernel",
+              "us": round(us, 2), "bytes": byt, "achieved_gbs": round(byt / us / 1e3, 1),
+              "peak_gbs": hbm, "frac": round(byt / us / 1e3 / hbm, 4), "bound": "hbm",
+              "l2": "flushed between launches"})
+        us_a = _time_us(lambda: ops.decode_attention(qkv.view(B, 3, H, D)[:, 0], kc, vc, lens, None,
+                                                     outb, ws), 20, flush)
+        emit({"op": "decode attention only (same state)", "kernel": "decode_split+combine",
+              "us": round(us_a, 2), "achieved_gbs": round(byt / us_a / 1e3, 1),
+              "frac": round(byt / us_a / 1e3 / hbm, 4), "bound": "hbm"})
+    return out
+
+
 def main():
     args = parse()
+    if args.suite == "ops":
+        run_ops(args)
+        return
     world, rank, local = dist_setup() if torch.cuda.is_available() else (1, 0, 0)
     if args.impl == "reference":
         try:

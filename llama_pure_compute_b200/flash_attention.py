@@ -23,9 +23,20 @@ from .ops import decode_attention
 __all__ = ["flash_attention_v2"]
 
 
+def _strides(t: torch.Tensor):
+    """(batch, head) strides in elements; size-1 dims get the packed value
+    (torch reports arbitrary strides for them)."""
+    b, h, s, d = t.shape
+    hs = t.stride(1) if h > 1 else s * d
+    bs = t.stride(0) if b > 1 else h * hs
+    return bs, hs
+
+
 def _kv_layout_ok(k: torch.Tensor, v: torch.Tensor) -> bool:
     D = k.shape[-1]
-    return (k.stride() == v.stride() and k.stride(-1) == 1 and k.stride(-2) == D
+    kb, kh = _strides(k)
+    return (_strides(v) == (kb, kh) and k.stride(-1) == 1 and (k.shape[2] == 1 or k.stride(-2) == D)
+            and kh >= k.shape[2] * D and kb >= k.shape[1] * kh
             and k.storage_offset() % 8 == 0 and v.storage_offset() % 8 == 0)
 
 
@@ -80,8 +91,9 @@ def flash_attention_v2(
         # one query per sequence: the whole prefix is visible, causal or not.
         # Read K/V in place when they are a sequence slice of a [B, H, S_max, D]
         # cache (row pitch S_max); otherwise pack them.
-        if k.stride(0) == hk * k.stride(1) and k.stride(1) % d == 0 and k.stride(1) >= kv_len * d:
-            smax = k.stride(1) // d
+        kb, kh = _strides(k)
+        if kb == hk * kh and kh % d == 0 and kh >= kv_len * d:
+            smax = kh // d
             shape = (bq, hk, smax, d)
             stride = (hk * smax * d, smax * d, d, 1)
             kc = k.as_strided(shape, stride)
@@ -95,7 +107,7 @@ def flash_attention_v2(
     out = torch.empty_like(q)
     rc = _lib.load().lpc_flash_attention(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), bq, hq, hk, q_len, kv_len, d,
-        k.stride(0), k.stride(1), 1 if causal else 0, float(sm_scale),
+        *_strides(k), 1 if causal else 0, float(sm_scale),
         _lib.dtype_code(q.dtype, "flash_attention"), _lib.stream_of(q))
     _lib.check(rc, "flash_attention")
     _lib.count_launch("lpc_flash_attention")

@@ -79,18 +79,25 @@ def rmsnorm_ref(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 
 
 def rmsswiglu_ref(x: torch.Tensor, w: torch.Tensor, gate_w: torch.Tensor, up_w: Optional[torch.Tensor],
-                  eps: float, compute: torch.dtype = torch.float32) -> torch.Tensor:
+                  eps: float, compute: torch.dtype = torch.float32,
+                  round_normed: bool = False) -> torch.Tensor:
     """RMSNorm -> gate/up -> silu(gate)*up in `compute` precision, cast back to
     x.dtype once: `_rmsswiglu_forward_pytorch` (src/llama_pure_compute/ops.py:45-59)
     evaluated the way tests/test_rmsswiglu_correctness.py:35-54 builds its
     ground truth.  up_w None/empty -> gate_w is the fused [2I, D] matrix
-    (src/csrc/ops/rmsswiglu.cu:167-173)."""
+    (src/csrc/ops/rmsswiglu.cu:167-173).
+
+    round_normed: store the normalised activations in x's dtype before the
+    projections, as the reference CUDA op does (rmsswiglu.cu:178-196 writes
+    x_normed with x's dtype and feeds it to the GEMM)."""
     if up_w is None or up_w.numel() == 0:
         inter = gate_w.shape[0] // 2
         gate_w, up_w = gate_w[:inter], gate_w[inter:]
     xf = x.to(compute)
     var = xf.pow(2).mean(-1, keepdim=True)
     xn = xf * torch.rsqrt(var + eps) * w.to(compute)
+    if round_normed:
+        xn = xn.to(x.dtype).to(compute)
     g = F.linear(xn, gate_w.to(compute))
     u = F.linear(xn, up_w.to(compute))
     return (F.silu(g) * u).to(x.dtype)
@@ -112,8 +119,8 @@ def attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: boo
         vf = vf.repeat_interleave(H // Hkv, dim=1)
     s = torch.matmul(q.float(), kf.transpose(-2, -1)) * sm_scale
     if causal:
-        qp = torch.arange(Skv - Sq, Skv).view(1, 1, Sq, 1)
-        kp = torch.arange(Skv).view(1, 1, 1, Skv)
+        qp = torch.arange(Skv - Sq, Skv, device=q.device).view(1, 1, Sq, 1)
+        kp = torch.arange(Skv, device=q.device).view(1, 1, 1, Skv)
         s = s.masked_fill(kp > qp, float("-inf"))
     p = torch.softmax(s, dim=-1)
     return torch.matmul(p, vf).to(q.dtype)
