@@ -175,6 +175,32 @@ LPC_API int lpc_decode_attention(const void* q, const void* key_cache, const voi
                          int head_dim, int64_t max_batch, int64_t max_seq_len, float sm_scale,
                          int dtype, void* stream);
 
+/*
+ * Decode attention that allocates nothing.  No counterpart in the reference:
+ * it is an addition for callers that cannot allocate device memory when they
+ * run attention -- a plugin whose host application owns all of HBM (e.g. a
+ * serving engine that reserves the free memory for its KV cache), or a
+ * serving loop that must never call cudaMalloc mid-request because the call
+ * can synchronise the device or fail under memory pressure.
+ * Same arguments and results as lpc_decode_attention, minus the workspace:
+ * the split partials go to a fixed scratch array of LPC_NOALLOC_SCRATCH_BYTES
+ * inside this library, held by every GPU that loads the library until the
+ * process exits.  Shapes whose partials need more
+ * (batch * heads * ceil(max_seq_len / 256) * (head_dim + 2) * 4 bytes) are
+ * rejected with LPC_ERR_INVALID before anything runs.
+ * The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture.
+ * All calls share the one array: calls that overlap on the GPU (two streams,
+ * or two host threads) race on it; serialise them.  Nothing in it needs to
+ * start at zero, each call writes every partial it reads.
+ */
+#define LPC_NOALLOC_SCRATCH_BYTES (24u * 1024u * 1024u)
+LPC_API int lpc_decode_attention_noalloc(const void* q, const void* key_cache,
+                                         const void* value_cache, const int32_t* seq_lens,
+                                         void* out, int64_t batch, int heads, int kv_heads,
+                                         int head_dim, int64_t max_batch, int64_t max_seq_len,
+                                         float sm_scale, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

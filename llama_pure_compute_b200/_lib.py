@@ -47,6 +47,8 @@ SIGNATURES = {
     "lpc_decode_attention_workspace_bytes": (_I64, [_I64, _I, _I64, _I]),
     "lpc_decode_attention": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _I64, _I64, _F,
                                   _I, _P]),
+    "lpc_decode_attention_noalloc": (_I, [_P, _P, _P, _P, _P, _I64, _I, _I, _I, _I64, _I64, _F, _I,
+                                          _P]),
 }
 
 _lib = None
@@ -56,7 +58,7 @@ _lock = threading.Lock()
 KERNELS_PER_CALL = {
     "lpc_update_kv_cache": 1, "lpc_rope_forward": 1, "lpc_rope_kv_append": 1,
     "lpc_rmsnorm_forward": 1, "lpc_rmsswiglu_forward": 2, "lpc_flash_attention": 1,
-    "lpc_decode_attention": 2,
+    "lpc_decode_attention": 2, "lpc_decode_attention_noalloc": 2,
 }
 launch_count = 0
 

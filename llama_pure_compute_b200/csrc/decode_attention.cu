@@ -427,3 +427,68 @@ extern "C" int lpc_decode_attention(const void* q, const void* key_cache, const 
     return launch_d<__half, 128>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, (int)max_splits, sl2, s);
   return launch_d<__half, 64>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, (int)max_splits, sl2, s);
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.
+//
+// Some callers cannot allocate device memory at the point where they run
+// decode attention: a plugin inside a host application that owns every byte
+// of HBM (for example a serving engine that reserves all free memory for its
+// KV cache at start-up), or code on a serving path that must never call
+// cudaMalloc because an allocation may synchronise the device or fail under
+// memory pressure in the middle of a request.  For them the split partials
+// live in a fixed scratch array in this library's device memory instead of a
+// caller workspace.  Each GPU that loads the library holds this array
+// (LPC_NOALLOC_SCRATCH_BYTES) until the process exits.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[LPC_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};  // device address of the scratch array, per device ordinal
+}  // namespace
+
+extern "C" int lpc_decode_attention_noalloc(const void* q, const void* key_cache,
+                                            const void* value_cache, const int32_t* seq_lens,
+                                            void* out, int64_t batch, int heads, int kv_heads,
+                                            int head_dim, int64_t max_batch, int64_t max_seq_len,
+                                            float sm_scale, int dtype, void* stream) {
+  using namespace lpc;
+  const int64_t need = lpc_decode_attention_workspace_bytes(batch, heads, max_seq_len, head_dim);
+  if (need > (int64_t)LPC_NOALLOC_SCRATCH_BYTES) {
+    set_error("decode_attention_noalloc: this shape needs %lld bytes of split scratch but the "
+              "static scratch holds %lld (batch * heads * ceil(max_seq_len / 256) * "
+              "(head_dim + 2) * 4 must fit); call lpc_decode_attention with a workspace instead",
+              (long long)need, (long long)LPC_NOALLOC_SCRATCH_BYTES);
+    return LPC_ERR_INVALID;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("decode_attention_noalloc: cannot query the current CUDA device");
+    return LPC_ERR_CUDA;
+  }
+  void* scratch = nullptr;
+  {
+    // First call on a device: resolve the scratch array's device address with
+    // that device current (the symbol's host-side name is not a device pointer).
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
+      if (e != cudaSuccess || !p) {
+        set_error("decode_attention_noalloc: cudaGetSymbolAddress failed: %s",
+                  cudaGetErrorString(e));
+        return LPC_ERR_CUDA;
+      }
+      g_noalloc_addr[dev] = p;
+    }
+    scratch = g_noalloc_addr[dev];
+  }
+  // No clearing is needed: every partial the combine step reads is written by
+  // the split step of the same call.
+  return lpc_decode_attention(q, key_cache, value_cache, seq_lens, out, scratch,
+                              (int64_t)LPC_NOALLOC_SCRATCH_BYTES, batch, heads, kv_heads, head_dim,
+                              max_batch, max_seq_len, sm_scale, dtype, stream);
+}
