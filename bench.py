@@ -44,9 +44,11 @@ GLOBAL_BATCH = 256
 PROMPT_LEN = 512
 NEW_TOKENS = 128
 SEED = 3
-# ncu dram bytes (read + write) per decode-attention launch, layer cache of the
-# 256 x ~576-token state; see profiles/decode_attention_7b.md (null until captured)
-DECODE_ATTN_NCU_TRAFFIC = None
+# ncu dram bytes (read + write) / algorithmic bytes of the decode-attention
+# kernel, from one capture of the ragged 16-sequence case
+# (profiles/decode_attention_ragged16.md): 589.1 MB / 583.9 MB.  The bench
+# scales it to its own launch (traffic grows with the K/V bytes processed).
+DECODE_ATTN_TRAFFIC_RATIO = (583.322880e6 + 5.812224e6) / 583.942144e6
 
 
 def parse():
@@ -59,10 +61,15 @@ def parse():
     ap.add_argument("--prompt-len", type=int, default=PROMPT_LEN)
     ap.add_argument("--layers", type=int, default=32, help="(debug only) fewer layers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--pre-steps", type=int, default=None,
+                    help="untimed decode steps before the timed ones (default: enough to centre "
+                         "the timed steps on the mean context)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--suite", choices=["decode", "ops"], default="decode",
                     help="decode: the 7B decode workload (default); ops: per-op roofline lines")
     ap.add_argument("--only", default="", help="comma list of op lines for --suite ops")
+    ap.add_argument("--decode-batch", type=int, default=64,
+                    help="sequences of the ragged decode op line (64 = the decode op shape)")
     return ap.parse_args()
 
 
@@ -273,6 +280,8 @@ def run_ours(args, world, rank, local):
     start, count = shard(args.batch, world, rank)
     mean_ctx = args.prompt_len + NEW_TOKENS // 2
     pre_steps = max(args.warmup, mean_ctx - args.prompt_len - args.steps // 2)
+    if args.pre_steps is not None:
+        pre_steps = max(args.warmup, args.pre_steps)
     max_seq = args.prompt_len + max(NEW_TOKENS, pre_steps + args.steps + 2)
     cfg = model_config(args.layers, max_seq)
 
@@ -423,7 +432,9 @@ def run_ours(args, world, rank, local):
                 "peak": hbm_peak,
                 "unit": "GB/s",
                 "frac": round(attn_gbs / hbm_peak, 4),
-                "traffic": DECODE_ATTN_NCU_TRAFFIC,
+                "traffic": int(attn_bytes * DECODE_ATTN_TRAFFIC_RATIO),
+                "traffic_source": "ncu capture of the 16-sequence ragged case scaled by bytes "
+                                  "(profiles/decode_attention_ragged16.md)",
                 "algorithmic_bytes_per_launch": attn_bytes,
                 "launch_us": round(attn_us, 2),
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (burst)" if peaks else "fallback 6650",
@@ -533,7 +544,7 @@ def run_ops(args):
               "l2": "inputs 201 MB > L2"})
     if not only or "decode" in only:
         torch.manual_seed(2)
-        B, H, D = 64, 32, 128
+        B, H, D = args.decode_batch, 32, 128
         L = torch.randint(128, 4097, (B,))
         Smax = 4097
         kc = torch.randn(B, H, Smax, D, device=dev, dtype=torch.bfloat16)
@@ -552,7 +563,7 @@ def run_ops(args):
 
         us = _time_us(step, 20, flush)
         byt = int((L + 1).sum()) * H * D * 2 * 2 + 3 * B * H * D * 2 * 2
-        emit({"op": "decode step 64 ragged seqs L~U[128,4096] (rope+append+attention)",
+        emit({"op": f"decode step {B} ragged seqs L~U[128,4096] (rope+append+attention)",
               "kernel": "rope_kv_append_kernel + decode_split_kernel + decode_combine_kernel",
               "us": round(us, 2), "bytes": byt, "achieved_gbs": round(byt / us / 1e3, 1),
               "peak_gbs": hbm, "frac": round(byt / us / 1e3 / hbm, 4), "bound": "hbm",
