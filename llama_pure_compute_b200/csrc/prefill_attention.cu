@@ -6,25 +6,27 @@
 // tests/test_attention_correctness.py:10-76 and the causal prefill kernel of
 // src/llama_pure_compute/triton_kernels/flash_attention.py:88-432.
 //
-// One CTA per (128-query tile, head, batch); 6 warps:
-//   warp 4     TMA producer: Q tile once (two 64-column boxes), then K and V
-//              128-key tiles into 2-stage rings, 4-D tensor maps so rows past
-//              kv_len (or q_len) read as zeros.
-//   warp 5     TMEM allocator and single-thread tcgen05.mma issuer:
-//                S_j = Q K_j^T           (M=128, N=128, K=128: 8 instructions)
-//                O  += P_{j-1} V_{j-1}   (A = P from smem, B = V MN-major)
-//              S is double-buffered in TMEM so S_{j+1} runs while the softmax
-//              warps work on S_j.
-//   warps 0-3  softmax: thread r owns query row r (TMEM lane r).  Row max and
-//              exp2 in fp32 from tcgen05.ld of S; P rounded to bf16/fp16 and
-//              written into a 128-byte-swizzled smem tile that is the A operand
-//              of the PV MMA.  The running max only moves (and O in TMEM is
-//              rescaled) when a tile's max exceeds it by more than 2^8, so the
-//              O correction is rare; the result is the same softmax, only the
-//              reference point of the exponentials differs.  Epilogue: O / l.
-// TMEM: S0 cols [0,128), S1 [128,256), O [256,384) (512 allocated).
-// Causal tiles past the diagonal are skipped entirely; q tiles are scheduled
-// longest-first.
+// One CTA per (256 queries = two 128-row tiles, head, batch); 10 warps:
+//   warp 8     TMA producer: Q0/Q1 once (64-column boxes), then K and V
+//              128-key tiles into 2-stage rings (4-D tensor maps: rows past
+//              kv_len / q_len read as zeros).  K/V tiles serve both Q tiles.
+//   warp 9     TMEM allocator and single-thread tcgen05.mma issuer, per key tile j:
+//                S0 = Q0 K_j^T, S1 = Q1 K_j^T        (M=128, N=128, K=128)
+//                O0 += P0 V_j, O1 += P1 V_j          (A = P from TMEM, B = V, MN-major)
+//   warps 0-3  softmax for Q0, warps 4-7 softmax for Q1 (ping-pong: while one
+//              warpgroup exponentiates, the tensor core runs the other tile's
+//              MMAs).  Thread r of a warpgroup owns query row r (TMEM lane r):
+//              one tcgen05.ld of its 128 scores, row max and exp2 in fp32,
+//              P rounded to bf16/fp16 and stored back into the first 64
+//              columns of its own S buffer (two 16-bit values per column), the
+//              A operand of the PV MMA.  The running max moves (and O is
+//              rescaled in TMEM) only when a tile's max exceeds it by more
+//              than 2^8; the result is the same softmax, only the reference
+//              point of the exponentials differs.  Epilogue: O / l.
+// TMEM (512 columns): S0/P0 [0,128), S1/P1 [128,256), O0 [256,384), O1 [384,512).
+// MMAs issued by one thread execute in order, so S_t of key tile j+1 never
+// overwrites P_t of tile j before PV_t(j) has read it.
+// Causal key tiles past the diagonal are skipped; q blocks run longest first.
 #include <atomic>
 
 #include "lpc_common.cuh"
@@ -43,16 +45,19 @@ unsigned int lpc_status_prefill(bool clear) {
 
 namespace {
 
-constexpr int BQ = 128;       // queries per CTA (UMMA M)
-constexpr int BKV = 128;      // keys per tile (UMMA N of S, K of PV)
-constexpr int HD = 128;       // head dim
-constexpr int BOX = 64;       // 64 x 2 B = one 128-byte swizzle row
-constexpr int TILE_BYTES = BQ * HD * 2;          // 32 KB: Q, one K stage, one V stage, P
-constexpr int HALF_BYTES = TILE_BYTES / 2;       // one 64-column box
-constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 256;
+constexpr int BQ = 128;                   // queries per tile (UMMA M)
+constexpr int NQT = 2;                    // query tiles per CTA
+constexpr int BKV = 128;                  // keys per tile
+constexpr int HD = 128;                   // head dim
+constexpr int BOX = 64;                   // 64 x 2 B = one 128-byte swizzle row
+constexpr int TILE_BYTES = BQ * HD * 2;   // 32 KB: one Q tile, one K or V stage
+constexpr int HALF_BYTES = TILE_BYTES / 2;
+constexpr int KV_STAGES = 2;
+constexpr int SMEM_BYTES = (NQT + 2 * KV_STAGES) * TILE_BYTES + 1024 + 256;
+constexpr int NTHREADS = 320;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float LOG2E = 1.4426950408889634f;
-constexpr float RESCALE_THRESHOLD = 8.0f;        // log2 units
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 
 struct TmaDesc4 { alignas(64) unsigned char bytes[128]; };
 
@@ -86,71 +91,72 @@ __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
 
 struct Params {
   int64_t q_len, kv_len, offset;  // offset = kv_len - q_len
-  int heads, kv_heads, group, num_q_tiles;
+  int heads, kv_heads, group, num_q_blocks;
   float scale_log2;
   int causal;
 };
 
 template <typename T>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(NTHREADS, 1)
     flash_prefill_kernel(const __grid_constant__ TmaDesc4 tmQ, const __grid_constant__ TmaDesc4 tmK,
                          const __grid_constant__ TmaDesc4 tmV, T* __restrict__ out,
                          const Params p, uint32_t idesc_qk, uint32_t idesc_pv) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = lpc::smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
-  const uint32_t sQ = base;
-  const uint32_t sK = base + TILE_BYTES;          // 2 stages
-  const uint32_t sV = base + 3 * TILE_BYTES;      // 2 stages
-  const uint32_t sP = base + 5 * TILE_BYTES;
-  const uint32_t bars = base + 6 * TILE_BYTES;
-  const uint32_t q_full = bars + 0;
+  const uint32_t sQ = base;                                 // NQT tiles
+  const uint32_t sK = base + NQT * TILE_BYTES;              // KV_STAGES
+  const uint32_t sV = sK + KV_STAGES * TILE_BYTES;          // KV_STAGES
+  const uint32_t bars = sV + KV_STAGES * TILE_BYTES;
+  const uint32_t q_full = bars;
   auto k_full = [&](int s) { return bars + 8u * (1 + s); };
   auto k_empty = [&](int s) { return bars + 8u * (3 + s); };
   auto v_full = [&](int s) { return bars + 8u * (5 + s); };
   auto v_empty = [&](int s) { return bars + 8u * (7 + s); };
-  auto s_full = [&](int s) { return bars + 8u * (9 + s); };
-  auto s_empty = [&](int s) { return bars + 8u * (11 + s); };
-  const uint32_t p_full = bars + 8u * 13;
-  const uint32_t o_ready = bars + 8u * 14;
+  auto s_full = [&](int t) { return bars + 8u * (9 + t); };
+  auto p_full = [&](int t) { return bars + 8u * (11 + t); };
+  auto o_done = [&](int t) { return bars + 8u * (13 + t); };
   const uint32_t tmem_slot = bars + 8u * 15;
   volatile uint32_t* tmem_slot_ptr =
       reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = p.num_q_tiles - 1 - (int)blockIdx.x;  // longest causal rows first
+  const int qb = p.num_q_blocks - 1 - (int)blockIdx.x;  // longest causal rows first
   const int h = blockIdx.y;
   const int b = blockIdx.z;
   const int kvh = h / p.group;
-  const int64_t q0 = (int64_t)qt * BQ;
+  const int64_t q0 = (int64_t)qb * (NQT * BQ);
   const int64_t kv_tiles_all = (p.kv_len + BKV - 1) / BKV;
-  int64_t n_tiles = kv_tiles_all;
-  if (p.causal) {
-    const int64_t last_key = p.offset + q0 + BQ - 1;  // largest key any row of this tile may see
-    n_tiles = min(n_tiles, last_key / BKV + 1);
-  }
-  const int n = (int)n_tiles;
+  // key tiles each query tile needs (the later tile sees the most keys)
+  auto tiles_for = [&](int t) -> int {
+    int64_t n = kv_tiles_all;
+    if (p.causal) n = min(n, (p.offset + q0 + (int64_t)(t + 1) * BQ - 1) / BKV + 1);
+    return (int)n;
+  };
+  const int n_q0 = tiles_for(0);
+  const int n_all = tiles_for(1);
 
   if (threadIdx.x == 0) {
     lpc::mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < KV_STAGES; ++s) {
       lpc::mbar_init(k_full(s), 1);
       lpc::mbar_init(k_empty(s), 1);
       lpc::mbar_init(v_full(s), 1);
       lpc::mbar_init(v_empty(s), 1);
-      lpc::mbar_init(s_full(s), 1);
-      lpc::mbar_init(s_empty(s), 4);
     }
-    lpc::mbar_init(p_full, 4);
-    lpc::mbar_init(o_ready, 1);
+    for (int t = 0; t < NQT; ++t) {
+      lpc::mbar_init(s_full(t), 1);
+      lpc::mbar_init(p_full(t), 4);
+      lpc::mbar_init(o_done(t), 1);
+    }
     lpc::fence_mbar_init();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == 8 && lane == 0) {
     lpc::tma_prefetch_desc(&tmQ);
     lpc::tma_prefetch_desc(&tmK);
     lpc::tma_prefetch_desc(&tmV);
   }
-  if (warp == 5) {
+  if (warp == 9) {
     lpc::tmem_alloc(tmem_slot, TMEM_COLS);
     lpc::tmem_relinquish();
   }
@@ -158,18 +164,19 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   lpc::tc_fence_after();
   const uint32_t tmem = *tmem_slot_ptr;
-  const uint32_t tO = tmem + 256u;
   unsigned int* st = &g_prefill_status;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------- TMA producer ----------------
-    if (lane == 0 && n > 0) {
-      lpc::mbar_arrive_expect_tx(q_full, TILE_BYTES);
-      tma_load_4d(sQ, &tmQ, 0, (int)q0, h, b, q_full);
-      tma_load_4d(sQ + HALF_BYTES, &tmQ, BOX, (int)q0, h, b, q_full);
-      for (int j = 0; j < n; ++j) {
-        const int s = j & 1;
-        const uint32_t par = ((uint32_t)(j >> 1) & 1u) ^ 1u;
+    if (lane == 0 && n_all > 0) {
+      lpc::mbar_arrive_expect_tx(q_full, NQT * TILE_BYTES);
+      for (int t = 0; t < NQT; ++t) {
+        tma_load_4d(sQ + t * TILE_BYTES, &tmQ, 0, (int)(q0 + t * BQ), h, b, q_full);
+        tma_load_4d(sQ + t * TILE_BYTES + HALF_BYTES, &tmQ, BOX, (int)(q0 + t * BQ), h, b, q_full);
+      }
+      for (int j = 0; j < n_all; ++j) {
+        const int s = j % KV_STAGES;
+        const uint32_t par = ((uint32_t)(j / KV_STAGES) & 1u) ^ 1u;
         const int k0 = j * BKV;
         if (!lpc::mbar_wait(k_empty(s), par, st)) break;
         lpc::mbar_arrive_expect_tx(k_full(s), TILE_BYTES);
@@ -181,79 +188,85 @@ __global__ void __launch_bounds__(192, 1)
         tma_load_4d(sV + s * TILE_BYTES + HALF_BYTES, &tmV, BOX, k0, kvh, b, v_full(s));
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0 && n > 0) {
+    if (lane == 0 && n_all > 0) {
       bool ok = lpc::mbar_wait(q_full, 0, st);
-      auto do_pv = [&](int i) -> bool {
-        if (!lpc::mbar_wait(p_full, (uint32_t)i & 1u, st)) return false;
-        if (!lpc::mbar_wait(v_full(i & 1), (uint32_t)(i >> 1) & 1u, st)) return false;
-        lpc::tc_fence_after();
-        const uint32_t vb = sV + (i & 1) * TILE_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk) {
-          // A: P rows = queries, K = keys (K-major, two 64-key boxes)
-          const uint64_t ad =
-              lpc::smem_desc_sw128(sP + (kk >> 2) * HALF_BYTES, 16, 1024) + 2u * (kk & 3);
-          // B: V rows = keys (K), 64-dim boxes along N: LBO = box stride, SBO = 8 keys
-          const uint64_t bd = lpc::smem_desc_sw128(vb + kk * 16 * 128, HALF_BYTES, 1024);
-          lpc::umma_ss(tO, ad, bd, idesc_pv, (i | kk) != 0);
-        }
-        lpc::umma_commit(v_empty(i & 1));
-        lpc::umma_commit(o_ready);
-        return true;
-      };
-      for (int j = 0; j < n && ok; ++j) {
-        const int s = j & 1;
-        if (!lpc::mbar_wait(k_full(s), (uint32_t)(j >> 1) & 1u, st)) { ok = false; break; }
-        if (j >= 2 && !lpc::mbar_wait(s_empty(s), (uint32_t)((j - 2) >> 1) & 1u, st)) { ok = false; break; }
+      for (int j = 0; j < n_all && ok; ++j) {
+        const int s = j % KV_STAGES;
+        const uint32_t spar = (uint32_t)(j / KV_STAGES) & 1u;
+        if (!lpc::mbar_wait(k_full(s), spar, st)) { ok = false; break; }
         lpc::tc_fence_after();
         const uint32_t kb = sK + s * TILE_BYTES;
+        for (int t = 0; t < NQT; ++t) {
+          if (t == 0 && j >= n_q0) continue;
+          const uint32_t qt = sQ + t * TILE_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint64_t ad =
-              lpc::smem_desc_sw128(sQ + (kk >> 2) * HALF_BYTES, 16, 1024) + 2u * (kk & 3);
-          const uint64_t bd =
-              lpc::smem_desc_sw128(kb + (kk >> 2) * HALF_BYTES, 16, 1024) + 2u * (kk & 3);
-          lpc::umma_ss((tmem + 128u * (uint32_t)s), ad, bd, idesc_qk, kk != 0);
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint64_t ad =
+                lpc::smem_desc_sw128(qt + (kk >> 2) * HALF_BYTES, 16, 1024) + 2u * (kk & 3);
+            const uint64_t bd =
+                lpc::smem_desc_sw128(kb + (kk >> 2) * HALF_BYTES, 16, 1024) + 2u * (kk & 3);
+            lpc::umma_ss(tmem + 128u * t, ad, bd, idesc_qk, kk != 0);
+          }
+          lpc::umma_commit(s_full(t));
         }
-        lpc::umma_commit(s_full(s));
         lpc::umma_commit(k_empty(s));
-        if (j >= 1 && !do_pv(j - 1)) { ok = false; break; }
+        if (!lpc::mbar_wait(v_full(s), spar, st)) { ok = false; break; }
+        const uint32_t vb = sV + s * TILE_BYTES;
+        for (int t = 0; t < NQT; ++t) {
+          if (t == 0 && j >= n_q0) continue;
+          if (!lpc::mbar_wait(p_full(t), (uint32_t)j & 1u, st)) { ok = false; break; }
+          lpc::tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk) {
+            // A: P_t in TMEM (16 keys = 8 columns of packed pairs); B: V rows = keys
+            const uint64_t bd = lpc::smem_desc_sw128(vb + kk * 16 * 128, HALF_BYTES, 1024);
+            lpc::umma_ts(tmem + 256u + 128u * t, tmem + 128u * t + 8u * kk, bd, idesc_pv,
+                         (j | kk) != 0);
+          }
+          lpc::umma_commit(o_done(t));
+        }
+        lpc::umma_commit(v_empty(s));
       }
-      if (ok) do_pv(n - 1);
     }
   } else {
-    // ---------------- softmax + epilogue (warps 0-3) ----------------
-    const int r = warp * 32 + lane;          // query row within the tile
-    const int64_t qpos = p.offset + q0 + r;  // absolute position of this query
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    // ---------------- softmax + epilogue: warpgroup t = warp / 4 ----------------
+    const int t = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;          // row within the query tile = TMEM lane
+    const int64_t qrow = q0 + (int64_t)t * BQ + r;  // query index
+    const int64_t qpos = p.offset + qrow;           // absolute position
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + 128u * t + lane_off;
+    const uint32_t tO = tmem + 256u + 128u * t + lane_off;
+    const int n = t == 0 ? n_q0 : n_all;
+    const int64_t lim = p.causal ? min(qpos, p.kv_len - 1) : p.kv_len - 1;  // last visible key
     float m_used = -INFINITY, l = 0.f;
     bool ok = n > 0;
     for (int j = 0; j < n && ok; ++j) {
-      const int s = j & 1;
-      if (!lpc::mbar_wait(s_full(s), (uint32_t)(j >> 1) & 1u, st)) { ok = false; break; }
+      if (!lpc::mbar_wait(s_full(t), (uint32_t)j & 1u, st)) { ok = false; break; }
       lpc::tc_fence_after();
       const int64_t k0 = (int64_t)j * BKV;
-      const bool need_mask = (k0 + BKV > p.kv_len) || (p.causal && k0 + BKV - 1 > p.offset + q0);
-      const int64_t lim = p.causal ? min(qpos, p.kv_len - 1) : p.kv_len - 1;  // last visible key
-      // pass 1: row max
-      float mt = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < BKV; c += 32) {
-        uint32_t v[32];
-        lpc::tmem_ld32((tmem + 128u * (uint32_t)s) + lane_off + c, v);
-        lpc::tmem_wait_ld();
+      const bool need_mask =
+          (k0 + BKV > p.kv_len) || (p.causal && k0 + BKV - 1 > p.offset + q0 + (int64_t)t * BQ);
+      uint32_t sv[BKV];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float x = __uint_as_float(v[i]);
-          if (need_mask && k0 + c + i > lim) x = -INFINITY;
-          mt = fmaxf(mt, x);
+      for (int c = 0; c < BKV; c += 32)
+        lpc::tmem_ld32(tS + c, *reinterpret_cast<uint32_t(*)[32]>(&sv[c]));
+      lpc::tmem_wait_ld();
+      float mt = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < BKV; ++i) {
+        float x = __uint_as_float(sv[i]);
+        if (need_mask && k0 + i > lim) {
+          x = -INFINITY;
+          sv[i] = __float_as_uint(x);
         }
+        mt = fmaxf(mt, x);
       }
       mt *= p.scale_log2;  // scale > 0
-      // wait for PV_{j-1}: P buffer free and O stable
-      if (j >= 1 && !lpc::mbar_wait(o_ready, (uint32_t)(j - 1) & 1u, st)) { ok = false; break; }
+      // PV_t(j-1) must be done: its P shares these TMEM columns and O must be stable
+      if (j >= 1 && !lpc::mbar_wait(o_done(t), (uint32_t)(j - 1) & 1u, st)) { ok = false; break; }
       lpc::tc_fence_after();
       float alpha = 1.f;
       bool rescale = false;
@@ -265,71 +278,46 @@ __global__ void __launch_bounds__(192, 1)
         rescale = true;
       }
       const float m_use = m_used == -INFINITY ? 0.f : m_used;
-      // pass 2: P = exp2(S*scale - m), row sum, bf16 P into the swizzled smem tile
       float rs = 0.f;
-      const uint32_t prow = sP + (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < BKV; c += 32) {
-        uint32_t v[32];
-        lpc::tmem_ld32((tmem + 128u * (uint32_t)s) + lane_off + c, v);
-        lpc::tmem_wait_ld();
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          float x0 = __uint_as_float(v[i]), x1 = __uint_as_float(v[i + 1]);
-          float e0 = fast_exp2(fmaf(x0, p.scale_log2, -m_use));
-          float e1 = fast_exp2(fmaf(x1, p.scale_log2, -m_use));
-          if (need_mask) {
-            if (k0 + c + i > lim) e0 = 0.f;
-            if (k0 + c + i + 1 > lim) e1 = 0.f;
-          }
+          const float e0 = fast_exp2(fmaf(__uint_as_float(sv[c + i]), p.scale_log2, -m_use));
+          const float e1 = fast_exp2(fmaf(__uint_as_float(sv[c + i + 1]), p.scale_log2, -m_use));
           rs += e0 + e1;
           pk[i >> 1] = pack2<T>(e0, e1);
         }
-        // 32 keys = 4 chunks of 16 bytes; chunk index within the 64-key box
-        const uint32_t box = sP + (uint32_t)(c >> 6) * HALF_BYTES;
-        const uint32_t rowb = box - sP + prow;
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const uint32_t chunk = (uint32_t)((c & 63) >> 3) + q4;
-          const uint32_t addr = rowb + ((chunk ^ (uint32_t)(r & 7)) << 4);
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * q4]),
-                       "r"(pk[4 * q4 + 1]), "r"(pk[4 * q4 + 2]), "r"(pk[4 * q4 + 3])
-                       : "memory");
-        }
+        lpc::tmem_st16(tS + (uint32_t)(c >> 1), pk);
       }
       l = l * alpha + rs;
-      lpc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) lpc::mbar_arrive(s_empty(s));
-      // rare: move O to the new reference max (warp-collective TMEM access)
       if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
         for (int c = 0; c < HD; c += 16) {
           uint32_t v[16];
-          lpc::tmem_ld16(tO + lane_off + c, v);
+          lpc::tmem_ld16(tO + c, v);
           lpc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-          lpc::tmem_st16(tO + lane_off + c, v);
+          lpc::tmem_st16(tO + c, v);
         }
-        lpc::tmem_wait_st();
       }
-      lpc::fence_proxy_async_smem();
+      lpc::tmem_wait_st();
       lpc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) lpc::mbar_arrive(p_full);
+      if (lane == 0) lpc::mbar_arrive(p_full(t));
     }
     // epilogue: O / l
-    if (ok && lpc::mbar_wait(o_ready, (uint32_t)(n - 1) & 1u, st)) {
+    if (ok && lpc::mbar_wait(o_done(t), (uint32_t)(n - 1) & 1u, st)) {
       lpc::tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      const bool valid = q0 + r < p.q_len;
-      T* orow = out + (((int64_t)b * p.heads + h) * p.q_len + q0 + r) * HD;
+      const bool valid = qrow < p.q_len;
+      T* orow = out + (((int64_t)b * p.heads + h) * p.q_len + qrow) * HD;
 #pragma unroll 1
       for (int c = 0; c < HD; c += 32) {
         uint32_t v[32];
-        lpc::tmem_ld32(tO + lane_off + c, v);
+        lpc::tmem_ld32(tO + c, v);
         lpc::tmem_wait_ld();
         if (valid) {
           uint32_t pk[16];
@@ -346,7 +334,7 @@ __global__ void __launch_bounds__(192, 1)
   }
   lpc::tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     lpc::tc_fence_after();
     lpc::tmem_dealloc(tmem, TMEM_COLS);
   }
@@ -417,25 +405,25 @@ extern "C" int lpc_flash_attention(const void* q, const void* k, const void* v, 
   p.heads = heads;
   p.kv_heads = kv_heads;
   p.group = heads / kv_heads;
-  p.num_q_tiles = (int)((q_len + BQ - 1) / BQ);
+  p.num_q_blocks = (int)((q_len + NQT * BQ - 1) / (NQT * BQ));
   p.scale_log2 = sm_scale * LOG2E;
   p.causal = causal ? 1 : 0;
   const uint32_t fmt = dtype == LPC_DTYPE_BF16 ? 1u : 0u;
   const uint32_t id_qk = idesc_f16(fmt, BQ, BKV, 0u, 0u);
   const uint32_t id_pv = idesc_f16(fmt, BQ, HD, 0u, 1u);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  dim3 grid((unsigned)p.num_q_tiles, (unsigned)heads, (unsigned)batch);
+  dim3 grid((unsigned)p.num_q_blocks, (unsigned)heads, (unsigned)batch);
   int rc;
   if (dtype == LPC_DTYPE_BF16) {
     static std::atomic<uint64_t> mask{0};
     if ((rc = once_per_device_smem((const void*)flash_prefill_kernel<__nv_bfloat16>, SMEM_BYTES, mask)))
       return rc;
-    flash_prefill_kernel<__nv_bfloat16><<<grid, 192, SMEM_BYTES, s>>>(tq, tk, tv, (__nv_bfloat16*)out, p, id_qk, id_pv);
+    flash_prefill_kernel<__nv_bfloat16><<<grid, NTHREADS, SMEM_BYTES, s>>>(tq, tk, tv, (__nv_bfloat16*)out, p, id_qk, id_pv);
   } else {
     static std::atomic<uint64_t> mask{0};
     if ((rc = once_per_device_smem((const void*)flash_prefill_kernel<__half>, SMEM_BYTES, mask)))
       return rc;
-    flash_prefill_kernel<__half><<<grid, 192, SMEM_BYTES, s>>>(tq, tk, tv, (__half*)out, p, id_qk, id_pv);
+    flash_prefill_kernel<__half><<<grid, NTHREADS, SMEM_BYTES, s>>>(tq, tk, tv, (__half*)out, p, id_qk, id_pv);
   }
   return check_launch("flash_attention");
 }
