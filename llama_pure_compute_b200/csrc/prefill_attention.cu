@@ -76,6 +76,31 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Packed fp32 pairs (Blackwell f32x2 FMA/ADD: two lanes of work per instruction).
+__device__ __forceinline__ uint64_t pack_f2(float lo, float hi) {
+  return ((uint64_t)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ uint64_t pack_u2(uint32_t lo, uint32_t hi) {
+  return ((uint64_t)hi << 32) | lo;
+}
+__device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t fma_f2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add_f2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
 template <>
@@ -190,44 +215,57 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
+    // Issue order per key tile j:  PV0(j), S0(j+1), PV1(j), S1(j+1).  While
+    // warpgroup 0 exponentiates S0(j+1) the tensor core runs PV1(j) and
+    // S1(j+1), and the other way round: the two softmax warpgroups alternate
+    // with the tensor core instead of waiting for it together.
     if (lane == 0 && n_all > 0) {
       bool ok = lpc::mbar_wait(q_full, 0, st);
-      for (int j = 0; j < n_all && ok; ++j) {
+      auto issue_s = [&](int t, int j) -> bool {
         const int s = j % KV_STAGES;
-        const uint32_t spar = (uint32_t)(j / KV_STAGES) & 1u;
-        if (!lpc::mbar_wait(k_full(s), spar, st)) { ok = false; break; }
+        if (!lpc::mbar_wait(k_full(s), (uint32_t)(j / KV_STAGES) & 1u, st)) return false;
         lpc::tc_fence_after();
         const uint32_t kb = sK + s * TILE_BYTES;
-        for (int t = 0; t < NQT; ++t) {
-          if (t == 0 && j >= n_q0) continue;
-          const uint32_t qt = sQ + t * TILE_BYTES;
+        const uint32_t qt = sQ + t * TILE_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint64_t ad =
-                lpc::smem_desc_sw128(qt + (kk >> 2) * HALF_BYTES, 16, 1024) + 2u * (kk & 3);
-            const uint64_t bd =
-                lpc::smem_desc_sw128(kb + (kk >> 2) * HALF_BYTES, 16, 1024) + 2u * (kk & 3);
-            lpc::umma_ss(tmem + 128u * t, ad, bd, idesc_qk, kk != 0);
-          }
-          lpc::umma_commit(s_full(t));
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint64_t ad =
+              lpc::smem_desc_sw128(qt + (kk >> 2) * HALF_BYTES, 16, 1024) + 2u * (kk & 3);
+          const uint64_t bd =
+              lpc::smem_desc_sw128(kb + (kk >> 2) * HALF_BYTES, 16, 1024) + 2u * (kk & 3);
+          lpc::umma_ss(tmem + 128u * t, ad, bd, idesc_qk, kk != 0);
         }
-        lpc::umma_commit(k_empty(s));
-        if (!lpc::mbar_wait(v_full(s), spar, st)) { ok = false; break; }
+        lpc::umma_commit(s_full(t));
+        return true;
+      };
+      auto issue_pv = [&](int t, int j) -> bool {
+        const int s = j % KV_STAGES;
+        if (!lpc::mbar_wait(p_full(t), (uint32_t)j & 1u, st)) return false;
+        if (!lpc::mbar_wait(v_full(s), (uint32_t)(j / KV_STAGES) & 1u, st)) return false;
+        lpc::tc_fence_after();
         const uint32_t vb = sV + s * TILE_BYTES;
-        for (int t = 0; t < NQT; ++t) {
-          if (t == 0 && j >= n_q0) continue;
-          if (!lpc::mbar_wait(p_full(t), (uint32_t)j & 1u, st)) { ok = false; break; }
-          lpc::tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk) {
-            // A: P_t in TMEM (16 keys = 8 columns of packed pairs); B: V rows = keys
-            const uint64_t bd = lpc::smem_desc_sw128(vb + kk * 16 * 128, HALF_BYTES, 1024);
-            lpc::umma_ts(tmem + 256u + 128u * t, tmem + 128u * t + 8u * kk, bd, idesc_pv,
-                         (j | kk) != 0);
-          }
-          lpc::umma_commit(o_done(t));
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          // A: P_t in TMEM (16 keys = 8 columns of packed pairs); B: V rows = keys
+          const uint64_t bd = lpc::smem_desc_sw128(vb + kk * 16 * 128, HALF_BYTES, 1024);
+          lpc::umma_ts(tmem + 256u + 128u * t, tmem + 128u * t + 8u * kk, bd, idesc_pv,
+                       (j | kk) != 0);
         }
-        lpc::umma_commit(v_empty(s));
+        lpc::umma_commit(o_done(t));
+        return true;
+      };
+      if (ok && n_q0 > 0) ok = issue_s(0, 0);
+      if (ok) ok = issue_s(1, 0);
+      if (ok) lpc::umma_commit(k_empty(0));
+      for (int j = 0; j < n_all && ok; ++j) {
+        if (j < n_q0 && !(ok = issue_pv(0, j))) break;
+        if (j + 1 < n_q0 && !(ok = issue_s(0, j + 1))) break;
+        if (!(ok = issue_pv(1, j))) break;
+        lpc::umma_commit(v_empty(j % KV_STAGES));
+        if (j + 1 < n_all) {
+          if (!(ok = issue_s(1, j + 1))) break;
+          lpc::umma_commit(k_empty((j + 1) % KV_STAGES));
+        }
       }
     }
   } else {
@@ -254,17 +292,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int c = 0; c < BKV; c += 32)
         lpc::tmem_ld32(tS + c, *reinterpret_cast<uint32_t(*)[32]>(&sv[c]));
       lpc::tmem_wait_ld();
-      float mt = -INFINITY;
+      if (need_mask) {
+        // keys k0 + i with i > lim - k0 are invisible to this row
+        const int lim_rel = (int)max((int64_t)-1, min(lim - k0, (int64_t)(BKV - 1)));
 #pragma unroll
-      for (int i = 0; i < BKV; ++i) {
-        float x = __uint_as_float(sv[i]);
-        if (need_mask && k0 + i > lim) {
-          x = -INFINITY;
-          sv[i] = __float_as_uint(x);
-        }
-        mt = fmaxf(mt, x);
+        for (int i = 0; i < BKV; ++i)
+          if (i > lim_rel) sv[i] = 0xff800000u;  // -inf
       }
-      mt *= p.scale_log2;  // scale > 0
+      float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < BKV; i += 4) {
+        m0 = max3(m0, __uint_as_float(sv[i]), __uint_as_float(sv[i + 1]));
+        m1 = max3(m1, __uint_as_float(sv[i + 2]), __uint_as_float(sv[i + 3]));
+      }
+      const float mt = fmaxf(m0, m1) * p.scale_log2;  // scale > 0
       // PV_t(j-1) must be done: its P shares these TMEM columns and O must be stable
       if (j >= 1 && !lpc::mbar_wait(o_done(t), (uint32_t)(j - 1) & 1u, st)) { ok = false; break; }
       lpc::tc_fence_after();
@@ -278,19 +319,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         rescale = true;
       }
       const float m_use = m_used == -INFINITY ? 0.f : m_used;
-      float rs = 0.f;
+      // e = exp2(s * scale - m) two at a time: packed fma, packed row-sum add
+      const uint64_t sc2 = pack_f2(p.scale_log2, p.scale_log2);
+      const uint64_t nm2 = pack_f2(-m_use, -m_use);
+      uint64_t rs2 = 0;
 #pragma unroll
       for (int c = 0; c < BKV; c += 32) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const float e0 = fast_exp2(fmaf(__uint_as_float(sv[c + i]), p.scale_log2, -m_use));
-          const float e1 = fast_exp2(fmaf(__uint_as_float(sv[c + i + 1]), p.scale_log2, -m_use));
-          rs += e0 + e1;
+          const uint64_t x2 = fma_f2(pack_u2(sv[c + i], sv[c + i + 1]), sc2, nm2);
+          const float e0 = fast_exp2(lo_f(x2));
+          const float e1 = fast_exp2(hi_f(x2));
+          const uint64_t e2 = pack_f2(e0, e1);
+          rs2 = add_f2(rs2, e2);
           pk[i >> 1] = pack2<T>(e0, e1);
         }
         lpc::tmem_st16(tS + (uint32_t)(c >> 1), pk);
       }
+      const float rs = lo_f(rs2) + hi_f(rs2);
       l = l * alpha + rs;
       if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1

@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(192, 1)
 // fp32 streaming path
 // ---------------------------------------------------------------------------
 constexpr int F32_ROWS = 8;
-constexpr int F32_WARPS = 8;
+constexpr int F32_WARPS = 16;
 
 template <typename W>
 __global__ void __launch_bounds__(F32_WARPS * 32, 1)
@@ -243,12 +243,14 @@ __global__ void __launch_bounds__(F32_WARPS * 32, 1)
 
   const int gw = blockIdx.x * F32_WARPS + warp;
   const int nwarps = gridDim.x * F32_WARPS;
-  for (int i = 2 * gw; i < I; i += 2 * nwarps) {
-    const bool two = i + 1 < I;
+  // rows gw, gw + nwarps, gw + 2*nwarps, ... taken two at a time
+  for (int i = gw; i < I; i += 2 * nwarps) {
+    const int i1 = i + nwarps;
+    const bool two = i1 < I;
     const float4* g0p = reinterpret_cast<const float4*>(wg + (int64_t)i * K);
     const float4* u0p = reinterpret_cast<const float4*>(wu + (int64_t)i * K);
-    const float4* g1p = two ? g0p + kv : g0p;
-    const float4* u1p = two ? u0p + kv : u0p;
+    const float4* g1p = two ? reinterpret_cast<const float4*>(wg + (int64_t)i1 * K) : g0p;
+    const float4* u1p = two ? reinterpret_cast<const float4*>(wu + (int64_t)i1 * K) : u0p;
     float ag0[F32_ROWS], au0[F32_ROWS], ag1[F32_ROWS], au1[F32_ROWS];
 #pragma unroll
     for (int r = 0; r < F32_ROWS; ++r) ag0[r] = au0[r] = ag1[r] = au1[r] = 0.f;
@@ -287,7 +289,7 @@ __global__ void __launch_bounds__(F32_WARPS * 32, 1)
         if (r == lane) { g0 = ag0[r]; u0 = au0[r]; g1 = ag1[r]; u1 = au1[r]; }
       float* orow = out + (m0 + lane) * I;
       orow[i] = (g0 / (1.0f + expf(-g0))) * u0;
-      if (two) orow[i + 1] = (g1 / (1.0f + expf(-g1))) * u1;
+      if (two) orow[i1] = (g1 / (1.0f + expf(-g1))) * u1;
     }
   }
 }
@@ -306,7 +308,7 @@ int launch_f32(const void* x, const void* nw, const void* gw, const void* uw, vo
   if (rcx) return rcx;
   const float* g = (const float*)gw;
   const float* u = uw ? (const float*)uw : g + (int64_t)I * K;
-  const int gx = std::max(1, std::min(lpc::current_device_sms(), (I + 2 * F32_WARPS - 1) / (2 * F32_WARPS)));
+  const int gx = std::max(1, std::min(lpc::current_device_sms(), (I + F32_WARPS - 1) / F32_WARPS));
   const int64_t gy = (M + F32_ROWS - 1) / F32_ROWS;
   dim3 grid((unsigned)gx, (unsigned)gy);
   kfn<<<grid, F32_WARPS * 32, smem, s>>>((const float*)x, (const W*)nw, g, u, (float*)out, M, K, I,
@@ -340,6 +342,7 @@ int launch_tc(const void* xn, const void* gw, const void* uw, void* out, int64_t
       ta, tg, tu, (T*)out, (int)M, K, I, up_off, num_m, num_n, idesc);
   return lpc::check_launch("rmsswiglu_forward (tcgen05)");
 }
+
 
 }  // namespace
 

@@ -64,19 +64,26 @@ class OracleLlama:
     holds them (model.py:363-373 buffers follow model.to(dtype))."""
 
     def __init__(self, cfg: Dict, sd: Dict[str, torch.Tensor], max_seq_len: int,
-                 table_dtype: torch.dtype = torch.float32):
+                 table_dtype: torch.dtype = torch.float32, dtype: torch.dtype = torch.float32,
+                 device: str = "cpu"):
+        """dtype/device: the arithmetic type and device of the evaluation
+        (fp32 on the CPU for the oracle proper; bf16 on a GPU gives a plain
+        per-op-rounded torch evaluation of the same graph, used only to size
+        the bf16 noise of a model in tests)."""
         self.cfg = cfg
-        self.w = {k: v.float() for k, v in sd.items()}
+        self.dtype = dtype
+        self.w = {k: v.to(device=device, dtype=dtype) for k, v in sd.items()}
         self.H, self.Hkv = cfg["num_heads"], cfg["num_kv_heads"]
         self.D = cfg["dim"] // self.H
         self.eps = cfg.get("rms_norm_eps", 1e-5)
         c, s = rope_tables(self.D, max_seq_len, cfg.get("rope_theta", 10000.0))
-        self.cos = c.to(table_dtype).float()
-        self.sin = s.to(table_dtype).float()
+        self.cos = c.to(table_dtype).to(device=device, dtype=dtype)
+        self.sin = s.to(table_dtype).to(device=device, dtype=dtype)
         self.L = cfg["num_layers"]
 
     def _norm(self, x, w):
-        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.eps) * w
+        xf = x.float()  # statistics in fp32 (rmsnorm.py:88-96), result in the working dtype
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps) * w.float()).to(self.dtype)
 
     def _rope(self, x, pos):
         h = self.D // 2
