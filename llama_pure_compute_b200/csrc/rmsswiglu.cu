@@ -16,7 +16,8 @@
 //                   (M=128, N=128, K=16 per instruction, fp32 accumulators)
 //        warps 0-3  epilogue: tcgen05.ld the gate and up columns of each token
 //                   row, silu(g)*u in fp32, one rounding to the output dtype
-//      6-stage smem ring, 32 KB per stage, mbarrier full/empty handshakes.
+//      smem ring of 32 KB (+16 KB per extra token tile) stages with mbarrier
+//      full/empty handshakes; ring depth and token tiles per CTA by size.
 //      Tiles are rasterised in groups of GROUP_M token tiles so that a wave of
 //      CTAs re-reads weight tiles from L2 rather than HBM.
 // fp32 path (CUDA cores, no TF32): each CTA normalises up to 8 token rows into
@@ -47,17 +48,17 @@ namespace {
 
 using lpc::Num;
 
-constexpr int BM = 128;          // tokens per tile (UMMA M)
+constexpr int BM = 128;          // tokens per MMA tile (UMMA M)
 constexpr int BNI = 64;          // inter columns per tile
 constexpr int BN = 2 * BNI;      // UMMA N: 64 gate rows + 64 up rows
 constexpr int BK = 64;           // 64 x 2 B = one 128-byte swizzle row
-constexpr int STAGES = 6;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int TC_SMEM = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr int GROUP_M = 16;
-constexpr uint32_t TMEM_COLS = 128;
+
+// Shared memory of one CTA holding MT token tiles and a STAGES-deep ring.
+template <int MT, int STAGES>
+constexpr int tc_smem() { return STAGES * (MT * A_BYTES + B_BYTES) + 1024 + 256; }
 
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
@@ -76,17 +77,21 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
   return __fdividef(g, 1.0f + __expf(-g)) * u;
 }
 
-template <typename T>
-__global__ void __launch_bounds__(192, 1)
+// MT token tiles (128 rows each) share every weight stage; STAGES-deep ring.
+template <typename T, int MT, int STAGES>
+__global__ void __launch_bounds__(192)
     swiglu_tc_kernel(const __grid_constant__ lpc::TmaDesc tmA,
                      const __grid_constant__ lpc::TmaDesc tmG,
                      const __grid_constant__ lpc::TmaDesc tmU, T* __restrict__ out, int M, int K,
                      int I, int up_row_off, int num_m, int num_n, uint32_t idesc) {
+  constexpr int A_STAGE = MT * A_BYTES;
+  constexpr int STAGE_BYTES = A_STAGE + B_BYTES;
+  constexpr uint32_t TMEM_COLS = MT * 128;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = lpc::smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   const uint32_t sA = base;
-  const uint32_t sB = base + STAGES * A_BYTES;
+  const uint32_t sB = base + STAGES * A_STAGE;
   const uint32_t bars = sB + STAGES * B_BYTES;
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
@@ -103,9 +108,9 @@ __global__ void __launch_bounds__(192, 1)
   const int first_m = group * GROUP_M;
   const int gm = min(GROUP_M, num_m - first_m);
   const int within = bid - group * GROUP_M * num_n;
-  const int mt = first_m + within % gm;
+  const int mt = first_m + within % gm;  // group of MT token tiles
   const int nt = within / gm;
-  const int m0 = mt * BM, i0 = nt * BNI;
+  const int m0 = mt * BM * MT, i0 = nt * BNI;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -137,7 +142,9 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t r = (uint32_t)(kb / STAGES);
         if (!lpc::mbar_wait(empty_bar(s), (r & 1u) ^ 1u, &g_swiglu_status)) break;
         lpc::mbar_arrive_expect_tx(full_bar(s), STAGE_BYTES);
-        lpc::tma_load_2d(sA + s * A_BYTES, &tmA, kb * BK, m0, full_bar(s));
+#pragma unroll
+        for (int t = 0; t < MT; ++t)
+          lpc::tma_load_2d(sA + s * A_STAGE + t * A_BYTES, &tmA, kb * BK, m0 + t * BM, full_bar(s));
         lpc::tma_load_2d(sB + s * B_BYTES, &tmG, kb * BK, i0, full_bar(s));
         lpc::tma_load_2d(sB + s * B_BYTES + B_BYTES / 2, &tmU, kb * BK, i0 + up_row_off,
                          full_bar(s));
@@ -150,11 +157,14 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t r = (uint32_t)(kb / STAGES);
         if (!lpc::mbar_wait(full_bar(s), r & 1u, &g_swiglu_status)) break;
         lpc::tc_fence_after();
-        const uint64_t ad = lpc::smem_desc_sw128(sA + s * A_BYTES, 16, 1024);
         const uint64_t bd = lpc::smem_desc_sw128(sB + s * B_BYTES, 16, 1024);
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)
-          lpc::umma_ss(tmem, ad + 2u * kk, bd + 2u * kk, idesc, (kb | kk) != 0);
+        for (int t = 0; t < MT; ++t) {
+          const uint64_t ad = lpc::smem_desc_sw128(sA + s * A_STAGE + t * A_BYTES, 16, 1024);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            lpc::umma_ss(tmem + 128u * t, ad + 2u * kk, bd + 2u * kk, idesc, (kb | kk) != 0);
+        }
         lpc::umma_commit(empty_bar(s));
       }
       lpc::umma_commit(accum_bar);
@@ -163,9 +173,11 @@ __global__ void __launch_bounds__(192, 1)
     // epilogue warps 0..3: TMEM lanes 32*warp .. 32*warp+31 = token rows
     const bool ok = lpc::mbar_wait(accum_bar, 0, &g_swiglu_status);
     lpc::tc_fence_after();
-    const int row = m0 + warp * 32 + lane;
-    const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
     if (ok) {
+#pragma unroll 1
+      for (int t = 0; t < MT; ++t) {
+      const int row = m0 + t * BM + warp * 32 + lane;
+      const uint32_t taddr = tmem + 128u * t + ((uint32_t)(warp * 32) << 16);
 #pragma unroll 1
       for (int c = 0; c < BNI; c += 16) {
         uint32_t g[16], u[16];
@@ -182,6 +194,7 @@ __global__ void __launch_bounds__(192, 1)
           dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
           dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
         }
+      }
       }
     }
   }
@@ -316,6 +329,28 @@ int launch_f32(const void* x, const void* nw, const void* gw, const void* uw, vo
   return lpc::check_launch("rmsswiglu_forward (fp32)");
 }
 
+template <typename T, int MT, int STAGES>
+int launch_tc_cfg(const lpc::TmaDesc& ta, const lpc::TmaDesc& tg, const lpc::TmaDesc& tu, void* out,
+                  int64_t M, int K, int I, int up_off, int dtype, cudaStream_t s) {
+  constexpr int smem = tc_smem<MT, STAGES>();
+  static std::atomic<uint64_t> mask{0};
+  int rc = lpc::once_per_device_smem((const void*)swiglu_tc_kernel<T, MT, STAGES>, smem, mask);
+  if (rc) return rc;
+  const int num_m = (int)((M + BM * MT - 1) / (BM * MT));  // groups of MT token tiles
+  const int num_n = (I + BNI - 1) / BNI;
+  const uint32_t idesc = lpc::idesc_f16(dtype == LPC_DTYPE_BF16 ? 1u : 0u, BM, BN, 0u, 0u);
+  swiglu_tc_kernel<T, MT, STAGES><<<(unsigned)((int64_t)num_m * num_n), 192, smem, s>>>(
+      ta, tg, tu, (T*)out, (int)M, K, I, up_off, num_m, num_n, idesc);
+  return lpc::check_launch("rmsswiglu_forward (tcgen05)");
+}
+
+// Tile shape by token count (measured on B200 for the 7B shape, 172 weight
+// tiles): decode-sized calls are weight-streaming and run best with every tile
+// resident at once -- two ~96 KB CTAs per SM (1 token tile x 3 stages at up to
+// 128 tokens: 56 us vs 64.5 us for one 192 KB CTA per SM; 2 token tiles x 2
+// stages at 256 tokens: 77 us vs 79 us).  Large calls (prefill) are
+// tensor-bound and keep one CTA per SM with a 6-deep ring.
+
 template <typename T>
 int launch_tc(const void* xn, const void* gw, const void* uw, void* out, int64_t M, int K, int I,
               int dtype, cudaStream_t s) {
@@ -331,18 +366,10 @@ int launch_tc(const void* xn, const void* gw, const void* uw, void* out, int64_t
     tu = tg;
     up_off = I;
   }
-  static std::atomic<uint64_t> tc_mask{0};
-  int rcx = lpc::once_per_device_smem((const void*)swiglu_tc_kernel<T>, TC_SMEM, tc_mask);
-  if (rcx) return rcx;
-  const int num_m = (int)((M + BM - 1) / BM);
-  const int num_n = (I + BNI - 1) / BNI;
-  const uint32_t idesc =
-      lpc::idesc_f16(dtype == LPC_DTYPE_BF16 ? 1u : 0u, BM, BN, 0u, 0u);
-  swiglu_tc_kernel<T><<<(unsigned)((int64_t)num_m * num_n), 192, TC_SMEM, s>>>(
-      ta, tg, tu, (T*)out, (int)M, K, I, up_off, num_m, num_n, idesc);
-  return lpc::check_launch("rmsswiglu_forward (tcgen05)");
+  if (M <= 128) return launch_tc_cfg<T, 1, 3>(ta, tg, tu, out, M, K, I, up_off, dtype, s);
+  if (M <= 256) return launch_tc_cfg<T, 2, 2>(ta, tg, tu, out, M, K, I, up_off, dtype, s);
+  return launch_tc_cfg<T, 1, 6>(ta, tg, tu, out, M, K, I, up_off, dtype, s);
 }
-
 
 }  // namespace
 
