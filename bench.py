@@ -531,6 +531,37 @@ def run_ops(args):
                   "us": round(us, 2), "bytes": byt, "achieved_gbs": round(byt / us / 1e3, 1),
                   "frac_hbm": round(byt / us / 1e3 / hbm, 4), "tflops": round(fl / us / 1e6, 1),
                   "frac_tc": round(fl / us / 1e6 / tc, 4), "l2": "flushed between launches"})
+    if not only or "wsgemm" in only:
+        from llama_pure_compute_b200.packed_linear import PackedWeight, packed_linear
+        # the projections of one 7B decode layer (+ lm_head) at decode-sized token counts
+        shapes = [("qkv", 12288, 4096, "store"), ("o_proj+resid", 4096, 4096, "residual"),
+                  ("gate_up swiglu", 11008, 4096, "swiglu"), ("down+resid", 4096, 11008, "residual"),
+                  ("lm_head", 32000, 4096, "store")]
+        for M in (256, 128, 32):
+            for name, n, k, epi in shapes:
+                g = torch.Generator(device=dev).manual_seed(n + k + M)
+                rows = 2 * n if epi == "swiglu" else n
+                w = (0.02 * torch.randn(rows, k, device=dev, generator=g)).to(torch.bfloat16)
+                x = torch.randn(M, k, device=dev, generator=g).to(torch.bfloat16)
+                pw = PackedWeight(w, layout="swiglu" if epi == "swiglu" else "linear")
+                h = torch.randn(M, n, device=dev, generator=g).to(torch.bfloat16)
+                if epi == "residual":
+                    fn = lambda: packed_linear(x, pw, "residual", resid=h, out=h)  # noqa: E731
+                    cub = lambda: torch.addmm(h, x, w.t())  # noqa: E731
+                elif epi == "swiglu":
+                    fn = lambda: packed_linear(x, pw, "swiglu")  # noqa: E731
+                    cub = lambda: torch.mm(x, w.t())  # noqa: E731
+                else:
+                    fn = lambda: packed_linear(x, pw)  # noqa: E731
+                    cub = lambda: torch.mm(x, w.t())  # noqa: E731
+                us = _time_us(fn, 20, flush)
+                us_cublas = _time_us(cub, 20, flush)
+                byt = rows * k * 2 + M * k * 2 + M * n * 2 * (2 if epi == "residual" else 1)
+                emit({"op": f"{name} M={M} [{rows},{k}]", "kernel": "wsgemm_kernel",
+                      "us": round(us, 2), "bytes": byt, "achieved_gbs": round(byt / us / 1e3, 1),
+                      "peak_gbs": hbm, "frac": round(byt / us / 1e3 / hbm, 4), "bound": "hbm",
+                      "cublas_us": round(us_cublas, 2), "l2": "flushed between launches"})
+                del w, pw
     if not only or "prefill" in only:
         torch.manual_seed(1)
         q, k, v = (torch.randn(4, 32, 2048, 128, device=dev).to(torch.bfloat16) for _ in range(3))

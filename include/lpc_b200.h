@@ -201,6 +201,40 @@ LPC_API int lpc_decode_attention_noalloc(const void* q, const void* key_cache,
                                          int head_dim, int64_t max_batch, int64_t max_seq_len,
                                          float sm_scale, int dtype, void* stream);
 
+/*
+ * Weight packing for the decode-sized GEMM below.  Run once per weight at
+ * model load.  The packed copy stores each 128-row x 64-k tile of the weight
+ * as one contiguous 16 KB block, already in the 128-byte-swizzled K-major
+ * layout that the tensor core reads from shared memory.
+ * layout 0: W0 [n_out, k] row-major (a linear layer's weight).
+ * layout 1: SwiGLU gate/up pair, n_out = intermediate size; gate rows from W0
+ *           [n_out, k] and up rows from W1 [n_out, k], or from W0 rows
+ *           n_out..2*n_out-1 when W1 is NULL (the fused gate_up layout that
+ *           rmsswiglu_forward accepts, ops.py:118-131).
+ * packed: lpc_packed_weight_bytes(n_out, k, layout) bytes, 16-byte aligned.
+ * k must be a multiple of 64; bf16 or fp16.
+ */
+LPC_API int64_t lpc_packed_weight_bytes(int64_t n_out, int k, int layout);
+LPC_API int lpc_pack_weights(const void* w0, const void* w1, void* packed, int64_t n_out, int k,
+                             int layout, int dtype, void* stream);
+
+/*
+ * Decode-sized GEMM against packed weights:
+ *   out[t, n] = epilogue(sum_k x[t, k] * W[n, k]),  t < tokens <= 256.
+ * Replaces: the gate/up GEMMs inside rmsswiglu_forward (ops.py:118-131) of a
+ *           decode step, once the norm has been applied (epilogue 2), and --
+ *           for wide layers such as lm_head (model.py:421) -- nn.Linear
+ *           projections (epilogues 0 and 1).  One CTA per 128-row weight tile:
+ *           meant for layers with about a hundred tiles or more.
+ * epilogue 0: out = acc                        (out [tokens, n_out])
+ * epilogue 1: out = resid + acc                (resid may equal out)
+ * epilogue 2: out = silu(x Wg^T) * (x Wu^T)    (packed with layout 1; out [tokens, n_out])
+ * x: [tokens, k] contiguous; fp32 accumulation, one rounding to the dtype.
+ * n_out <= 2^24.  No workspace.
+ */
+LPC_API int lpc_wsgemm(const void* x, const void* packed_w, void* out, const void* resid,
+                       int64_t tokens, int64_t n_out, int k, int epilogue, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

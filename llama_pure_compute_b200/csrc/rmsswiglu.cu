@@ -9,23 +9,31 @@
 //
 // bf16/fp16 path (tensor cores, sm_100a):
 //   1. row RMSNorm -> normalised activations in the caller's workspace (bf16)
-//   2. one warp-specialised tcgen05 GEMM per 128-token x 64-inter tile:
-//        warp 4     TMA producer: A = 128x64 activation tile, B = 64 gate rows
-//                   + 64 up rows (two TMA boxes into one 128-row operand)
-//        warp 5     TMEM allocator + single-thread tcgen05.mma issuer
-//                   (M=128, N=128, K=16 per instruction, fp32 accumulators)
-//        warps 0-3  epilogue: tcgen05.ld the gate and up columns of each token
-//                   row, silu(g)*u in fp32, one rounding to the output dtype
-//      smem ring of 32 KB (+16 KB per extra token tile) stages with mbarrier
-//      full/empty handshakes; ring depth and token tiles per CTA by size.
-//      Tiles are rasterised in groups of GROUP_M token tiles so that a wave of
-//      CTAs re-reads weight tiles from L2 rather than HBM.
+//   2. a warp-specialised tcgen05 GEMM with the SiLU*up epilogue, in one of
+//      two forms chosen by token count:
+//      * one CTA per 128-token x 64-inter tile (up to 128 tokens):
+//          warp 4     TMA producer: A = 128x64 activation tile, B = 64 gate rows
+//                     + 64 up rows (two TMA boxes into one 128-row operand)
+//          warp 5     TMEM allocator + single-thread tcgen05.mma issuer
+//                     (M=128, N=128, K=16 per instruction, fp32 accumulators)
+//          warps 0-3  epilogue: tcgen05.ld the gate and up columns of each token
+//                     row, silu(g)*u in fp32, one rounding to the output dtype
+//      * a CTA pair (cluster of 2, tcgen05 cta_group::2) per 256-token x
+//        128-inter tile (more than 128 tokens): M = 256 tokens split over the
+//        two CTAs, N = 128 gate rows (CTA 0) + 128 up rows (CTA 1); both CTAs'
+//        TMA copies complete on CTA 0's barrier, CTA 0 issues the pair MMA and
+//        each CTA's TMEM ends up holding its own tokens' gate|up accumulators.
+//      smem rings of 32 KB stages with mbarrier full/empty handshakes; tiles
+//      rasterised in groups of GROUP_M token tiles so that a wave of CTAs
+//      re-reads weight tiles from L2 rather than HBM.
 // fp32 path (CUDA cores, no TF32): each CTA normalises up to 8 token rows into
 //   shared memory, then streams gate/up rows with 16-byte loads and reduces the
 //   dot products per warp.  It is the weight-streaming (HBM-bound) GEMV of the
 //   fp32 op shape (8 tokens).
 #include <atomic>
 #include <mutex>
+
+#include <cstdlib>
 
 #include "lpc_common.cuh"
 
@@ -207,6 +215,158 @@ __global__ void __launch_bounds__(192)
 }
 
 // ---------------------------------------------------------------------------
+// CTA-pair kernel (cluster of 2, tcgen05 cta_group::2): one pair MMA of
+// M = 256 tokens (128 in each CTA's shared memory) by N = 256 weight rows
+// (128 gate rows in CTA 0, the 128 matching up rows in CTA 1).  Each CTA
+// streams 16 KB of weights + 16 KB of activations per 64-k stage, half the
+// activation bytes per weight byte of a one-CTA tile with 256 tokens, and each
+// CTA's TMEM receives its 128 tokens x (128 gate | 128 up) accumulators, so the
+// SiLU*up epilogue needs no exchange.
+//   warp 4     producer (own CTA's two TMA boxes per stage)
+//   warp 5     TMEM pair allocation; rank 0: MMA issuer
+// Both CTAs' TMA copies of a stage complete on rank 0's full barrier; rank 0
+// commits MMA completion to the empty / accumulator barriers of both CTAs.
+//   warps 0-3  epilogue (TMEM lane = token)
+// ---------------------------------------------------------------------------
+constexpr int PAIR_TOK = 256;     // tokens per pair tile
+constexpr int PAIR_I = 128;       // inter columns per pair tile
+constexpr int PAIR_STAGE = A_BYTES + PAIR_I * BK * 2;  // 16 KB tokens + 16 KB weights
+
+template <int STAGES>
+constexpr int pair_smem() { return STAGES * PAIR_STAGE + 1024 + 256; }
+
+template <typename T, int STAGES>
+__global__ void __launch_bounds__(192)
+    swiglu_pair_kernel(const __grid_constant__ lpc::TmaDesc tmA,
+                       const __grid_constant__ lpc::TmaDesc tmG,
+                       const __grid_constant__ lpc::TmaDesc tmU, T* __restrict__ out, int M, int K,
+                       int I, int up_row_off, int num_m, int num_p, uint32_t idesc) {
+  constexpr uint32_t TMEM_COLS = 2 * PAIR_I;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = lpc::smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;  // same offset in both CTAs of the pair
+  const uint32_t sA = base;
+  const uint32_t sB = base + STAGES * A_BYTES;
+  const uint32_t bars = sB + STAGES * (PAIR_I * BK * 2);
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
+  const uint32_t accum_bar = bars + 8u * (2 * STAGES);
+  const uint32_t tmem_slot = accum_bar + 8u;
+  volatile uint32_t* tmem_slot_ptr =
+      reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = lpc::cluster_ctarank();
+
+  // grouped rasterisation over (token tile, inter tile) pairs
+  const int pid = blockIdx.x >> 1;
+  const int group = pid / (GROUP_M * num_p);
+  const int first_m = group * GROUP_M;
+  const int gm = min(GROUP_M, num_m - first_m);
+  const int within = pid - group * GROUP_M * num_p;
+  const int mt = first_m + within % gm;
+  const int pt = within / gm;
+  const int m0 = mt * PAIR_TOK + (int)rank * BM;  // this CTA's 128 tokens
+  const int i0 = pt * PAIR_I;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      lpc::mbar_init(full_bar(s), 1);
+      lpc::mbar_init(empty_bar(s), 1);
+    }
+    lpc::mbar_init(accum_bar, 1);
+    lpc::fence_mbar_init();
+  }
+  if (warp == 4 && lane == 0) {
+    lpc::tma_prefetch_desc(&tmA);
+    lpc::tma_prefetch_desc(rank == 0 ? (const void*)&tmG : (const void*)&tmU);
+  }
+  lpc::cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrive
+  if (warp == 5) {
+    lpc::tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    lpc::tmem_relinquish_pair();
+  }
+  lpc::tc_fence_before();
+  __syncthreads();
+  lpc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot_ptr;
+  const int nkb = K / BK;
+  unsigned int* st = &g_swiglu_status;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      const lpc::TmaDesc* tw = rank == 0 ? &tmG : &tmU;
+      const int wrow = rank == 0 ? i0 : i0 + up_row_off;
+      // both CTAs' copies complete on rank 0's full barrier, armed by rank 0
+      // for the bytes of both halves
+      const uint32_t full0 = lpc::mapa_shared(full_bar(0), 0);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t r = (uint32_t)(kb / STAGES);
+        if (!lpc::mbar_wait(empty_bar(s), (r & 1u) ^ 1u, st)) break;
+        if (rank == 0) lpc::mbar_arrive_expect_tx(full_bar(s), 2 * PAIR_STAGE);
+        lpc::tma_load_2d_pair(sA + s * A_BYTES, &tmA, kb * BK, m0, full0 + 8u * s);
+        lpc::tma_load_2d_pair(sB + s * (PAIR_I * BK * 2), tw, kb * BK, wrow, full0 + 8u * s);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      if (rank == 0) {
+        const uint32_t peer_empty0 = lpc::mapa_shared(empty_bar(0), 1);
+        const uint32_t peer_accum = lpc::mapa_shared(accum_bar, 1);
+        for (int kb = 0; kb < nkb; ++kb) {
+          const int s = kb % STAGES;
+          const uint32_t par = (uint32_t)(kb / STAGES) & 1u;
+          if (!lpc::mbar_wait(full_bar(s), par, st)) break;
+          lpc::tc_fence_after();
+          const uint64_t ad = lpc::smem_desc_sw128(sA + s * A_BYTES, 16, 1024);
+          const uint64_t bd = lpc::smem_desc_sw128(sB + s * (PAIR_I * BK * 2), 16, 1024);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            lpc::umma_ss_pair(tmem, ad + 2u * kk, bd + 2u * kk, idesc, (kb | kk) != 0);
+          lpc::umma_commit_pair(empty_bar(s));
+          lpc::umma_commit_pair(peer_empty0 + 8u * s);
+        }
+        lpc::umma_commit_pair(accum_bar);
+        lpc::umma_commit_pair(peer_accum);
+      }
+    }
+  } else {
+    // epilogue warps 0..3: TMEM lanes 32*warp .. +31 = this CTA's tokens;
+    // columns 0..127 gate, 128..255 up, for inter columns i0 ..
+    const bool ok = lpc::mbar_wait(accum_bar, 0, st);
+    lpc::tc_fence_after();
+    if (ok) {
+      const int row = m0 + warp * 32 + lane;
+      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < PAIR_I; c += 16) {
+        uint32_t g[16], u[16];
+        lpc::tmem_ld16(taddr + c, g);
+        lpc::tmem_ld16(taddr + PAIR_I + c, u);
+        lpc::tmem_wait_ld();
+        if (row < M && i0 + c < I) {
+          uint32_t p[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            p[j] = pack2<T>(silu_mul(__uint_as_float(g[2 * j]), __uint_as_float(u[2 * j])),
+                            silu_mul(__uint_as_float(g[2 * j + 1]), __uint_as_float(u[2 * j + 1])));
+          uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)row * I + i0 + c);
+          dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
+          dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
+        }
+      }
+    }
+  }
+  lpc::tc_fence_before();
+  lpc::cluster_sync();  // the peer's shared memory and barriers outlive every pair MMA and arrive
+  if (warp == 5) {
+    lpc::tc_fence_after();
+    lpc::tmem_dealloc_pair(tmem, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // fp32 streaming path
 // ---------------------------------------------------------------------------
 constexpr int F32_ROWS = 8;
@@ -344,12 +504,61 @@ int launch_tc_cfg(const lpc::TmaDesc& ta, const lpc::TmaDesc& tg, const lpc::Tma
   return lpc::check_launch("rmsswiglu_forward (tcgen05)");
 }
 
-// Tile shape by token count (measured on B200 for the 7B shape, 172 weight
-// tiles): decode-sized calls are weight-streaming and run best with every tile
-// resident at once -- two ~96 KB CTAs per SM (1 token tile x 3 stages at up to
-// 128 tokens: 56 us vs 64.5 us for one 192 KB CTA per SM; 2 token tiles x 2
-// stages at 256 tokens: 77 us vs 79 us).  Large calls (prefill) are
-// tensor-bound and keep one CTA per SM with a 6-deep ring.
+// Tile shape by token count, measured on B200 for the 7B layer (dim 4096,
+// inter 11008) in steady state (launches back to back over weights larger
+// than L2):
+//   tokens        1-CTA 1x3   1-CTA 2x2   1-CTA 1x6   pair x3   pair x6
+//   32              44.2        63.3        53.8        55.4      61.6  us
+//   128             46.1        65.4        55.5        56.8      62.6
+//   256             69.8        69.1        74.2        59.5      65.3
+//   512             99.5       116.9       116.9        90.6      89.6
+//   2048           313.0       293.8       403.5       264.2     275.6
+// Up to 128 tokens the one-CTA tile with two ~96 KB CTAs per SM keeps every
+// weight tile streaming at once; beyond, the CTA pair halves the activation
+// bytes per weight byte (and the shared-memory operand traffic per MMA).
+// LPC_SWIGLU_CFG=1..5 forces a column of this table (measurement and tests).
+
+template <typename T, int STAGES>
+int launch_pair(const lpc::TmaDesc& ta, const void* gw, const void* uw, void* out, int64_t M, int K,
+                int I, int dtype, cudaStream_t s) {
+  lpc::TmaDesc tg, tu;
+  int rc, up_off = 0;
+  if (uw) {
+    if ((rc = lpc::make_tma_2d(&tg, gw, dtype, K, (uint64_t)I, (uint64_t)K * 2, BK, PAIR_I, true))) return rc;
+    if ((rc = lpc::make_tma_2d(&tu, uw, dtype, K, (uint64_t)I, (uint64_t)K * 2, BK, PAIR_I, true))) return rc;
+  } else {
+    if ((rc = lpc::make_tma_2d(&tg, gw, dtype, K, (uint64_t)2 * I, (uint64_t)K * 2, BK, PAIR_I, true))) return rc;
+    tu = tg;
+    up_off = I;
+  }
+  constexpr int smem = pair_smem<STAGES>();
+  static std::atomic<uint64_t> mask{0};
+  if ((rc = lpc::once_per_device_smem((const void*)swiglu_pair_kernel<T, STAGES>, smem, mask)))
+    return rc;
+  const int num_m = (int)((M + PAIR_TOK - 1) / PAIR_TOK);
+  const int num_p = (I + PAIR_I - 1) / PAIR_I;
+  const uint32_t idesc =
+      lpc::idesc_f16(dtype == LPC_DTYPE_BF16 ? 1u : 0u, PAIR_TOK, 2 * PAIR_I, 0u, 0u);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * (int64_t)num_m * num_p));
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, swiglu_pair_kernel<T, STAGES>, ta, tg, tu, (T*)out,
+                                     (int)M, K, I, up_off, num_m, num_p, idesc);
+  if (e != cudaSuccess) {
+    lpc::set_error("rmsswiglu_forward (tcgen05 pair): launch failed: %s", cudaGetErrorString(e));
+    return LPC_ERR_CUDA;
+  }
+  return lpc::check_launch("rmsswiglu_forward (tcgen05 pair)");
+}
 
 template <typename T>
 int launch_tc(const void* xn, const void* gw, const void* uw, void* out, int64_t M, int K, int I,
@@ -366,9 +575,15 @@ int launch_tc(const void* xn, const void* gw, const void* uw, void* out, int64_t
     tu = tg;
     up_off = I;
   }
+  const char* force = getenv("LPC_SWIGLU_CFG");  // tile-selection override for measurements
+  const int cfg = force ? atoi(force) : 0;
+  if (cfg == 1) return launch_tc_cfg<T, 1, 3>(ta, tg, tu, out, M, K, I, up_off, dtype, s);
+  if (cfg == 2) return launch_tc_cfg<T, 2, 2>(ta, tg, tu, out, M, K, I, up_off, dtype, s);
+  if (cfg == 3) return launch_tc_cfg<T, 1, 6>(ta, tg, tu, out, M, K, I, up_off, dtype, s);
+  if (cfg == 4) return launch_pair<T, 3>(ta, gw, uw, out, M, K, I, dtype, s);
+  if (cfg == 5) return launch_pair<T, 6>(ta, gw, uw, out, M, K, I, dtype, s);
   if (M <= 128) return launch_tc_cfg<T, 1, 3>(ta, tg, tu, out, M, K, I, up_off, dtype, s);
-  if (M <= 256) return launch_tc_cfg<T, 2, 2>(ta, tg, tu, out, M, K, I, up_off, dtype, s);
-  return launch_tc_cfg<T, 1, 6>(ta, tg, tu, out, M, K, I, up_off, dtype, s);
+  return launch_pair<T, 3>(ta, gw, uw, out, M, K, I, dtype, s);
 }
 
 }  // namespace

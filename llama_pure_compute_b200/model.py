@@ -14,7 +14,9 @@ checkpoints and call sites carry over.  What runs underneath:
                        prefill / no cache: lpc_flash_attention (tcgen05)
   o_proj + residual -> one addmm (residual added in the GEMM epilogue)
   post norm + SwiGLU-> lpc_rmsswiglu_forward (model.py:315-321; tcgen05 GEMM
-                       with the SiLU*up epilogue, no torch.cat of weights)
+                       with the SiLU*up epilogue, no torch.cat of weights);
+                       decode steps of <= 128 tokens: lpc_rmsnorm_forward +
+                       lpc_wsgemm on a packed copy of gate/up
   down + residual   -> one addmm
   lm_head           -> all positions by default (model.py:475), or only the
                        last one with ``last_token_only=True``
@@ -36,6 +38,10 @@ from .flash_attention import flash_attention_v2
 from .kv_manager import KVCacheManager
 from .ops import decode_attention, rmsswiglu_forward, rope_forward
 from .rmsnorm import RMSNorm
+
+# Decode steps with at most this many tokens run the SwiGLU GEMM on packed
+# weights (lpc_wsgemm); the packed copy of gate/up is built on first use.
+PACKED_SWIGLU_MAX_TOKENS = 128
 
 __all__ = ["precompute_freqs_cis", "LlamaAttention", "LlamaDecodeLayer", "LlamaModel",
            "LlamaForCausalLM"]
@@ -165,6 +171,35 @@ class LlamaDecodeLayer(nn.Module):
         self.gate_proj = nn.Linear(config.dim, config.inter_dim, bias=False)
         self.up_proj = nn.Linear(config.dim, config.inter_dim, bias=False)
         self.down_proj = nn.Linear(config.inter_dim, config.dim, bias=False)
+        self._packed_gate_up = None
+        self._packed_key = None
+
+    def packed_gate_up(self):
+        """gate/up weights in the packed SwiGLU tile layout (lpc_pack_weights),
+        built on first use and rebuilt when either weight changes."""
+        from .packed_linear import PackedWeight
+        ws = (self.gate_proj.weight, self.up_proj.weight)
+        key = tuple((w.data_ptr(), w._version, w.dtype, w.device) for w in ws)
+        if self._packed_gate_up is None or key != self._packed_key:
+            self._packed_gate_up = PackedWeight(ws[0], ws[1], layout="swiglu")
+            self._packed_key = key
+        return self._packed_gate_up
+
+    def _mlp_inter(self, h: torch.Tensor, decode: bool) -> torch.Tensor:
+        norm = self.post_attention_layernorm
+        tokens = h.numel() // h.shape[-1]
+        w = self.gate_proj.weight
+        if (decode and tokens <= PACKED_SWIGLU_MAX_TOKENS and h.dtype in (torch.bfloat16, torch.float16)
+                and w.dtype == h.dtype and h.shape[-1] % 64 == 0):
+            # decode-sized: norm, then the weight-streaming GEMM on packed
+            # weights with the SiLU*up epilogue (faster than the activation-
+            # major tile of the fused op at these token counts)
+            from .ops import rmsnorm_forward
+            from .packed_linear import packed_linear
+            normed = rmsnorm_forward(h, norm.weight, norm.eps)
+            return packed_linear(normed, self.packed_gate_up(), "swiglu")
+        return rmsswiglu_forward(h, rms_weight=norm.weight, gate_w=self.gate_proj.weight,
+                                 up_w=self.up_proj.weight, eps=norm.eps)
 
     def forward(
         self,
@@ -180,9 +215,7 @@ class LlamaDecodeLayer(nn.Module):
         attn = self.self_attn(self.input_layernorm(x), positions=positions, cos=cos, sin=sin,
                               kv_cache=kv_cache, layer_idx=self.layer_idx, mask=mask, ctx=ctx)
         h = self.self_attn.project_out(attn, x)
-        mlp_inter = rmsswiglu_forward(h, rms_weight=self.post_attention_layernorm.weight,
-                                      gate_w=self.gate_proj.weight, up_w=self.up_proj.weight,
-                                      eps=self.post_attention_layernorm.eps)
+        mlp_inter = self._mlp_inter(h, ctx is not None and ctx.decode)
         shp = h.shape
         return torch.addmm(h.reshape(-1, shp[-1]), mlp_inter.reshape(-1, mlp_inter.shape[-1]),
                            self.down_proj.weight.t()).view(shp)

@@ -277,6 +277,28 @@ def test_rmsswiglu_ragged_token_counts(M):
     half_ulp_bar(y, ref, torch.bfloat16, f"rmsswiglu M={M}")
 
 
+@pytest.mark.parametrize("cfg", [1, 2, 3, 4, 5])
+@pytest.mark.parametrize("M,D,I,fused", [(1, 1024, 320, False), (129, 1024, 320, True),
+                                         (256, 4096, 11008, False), (300, 512, 1024, True)])
+def test_rmsswiglu_every_tile_config(monkeypatch, cfg, M, D, I, fused):
+    """Every GEMM tile configuration (LPC_SWIGLU_CFG: 1 / 2 / 3 one-CTA tiles
+    with 1, 2 or 1 token tiles, 4 / 5 CTA-pair tiles with 3- and 6-deep rings)
+    against the oracle, and bit-identical to the default choice."""
+    g = torch.Generator(device=DEV).manual_seed(M + I)
+    x = torch.randn(M, D, device=DEV, generator=g).to(torch.bfloat16)
+    w = (1 + 0.02 * torch.randn(D, device=DEV, generator=g)).to(torch.bfloat16)
+    gw = (torch.randn(I, D, device=DEV, generator=g) / D ** 0.5).to(torch.bfloat16)
+    uw = (torch.randn(I, D, device=DEV, generator=g) / D ** 0.5).to(torch.bfloat16)
+    args = (torch.cat([gw, uw]), torch.empty(0, device=DEV, dtype=torch.bfloat16)) if fused else (gw, uw)
+    y_default = ops.rmsswiglu_forward(x, w, *args, 1e-5)
+    monkeypatch.setenv("LPC_SWIGLU_CFG", str(cfg))
+    y = ops.rmsswiglu_forward(x, w, *args, 1e-5)
+    monkeypatch.delenv("LPC_SWIGLU_CFG")
+    ref = rmsswiglu_ref(x, w, gw, uw, 1e-5, round_normed=True)
+    half_ulp_bar(y, ref, torch.bfloat16, f"rmsswiglu cfg={cfg} M={M}")
+    assert torch.equal(y, y_default), f"cfg {cfg} differs from the default tile choice"
+
+
 # ---------------------------------------------------------------------------
 # Attention
 # ---------------------------------------------------------------------------
