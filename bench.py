@@ -356,7 +356,7 @@ def run_ours(args, world, rank, local):
     # final decode state (layer 0 cache, current per-sequence lengths) ----
     lens = kv.seq_lens[:B].clone()
     q = torch.randn(B, cfg.num_heads, cfg.head_dim, device=dev, dtype=torch.bfloat16)
-    ws = model.model._workspace(B, kv.max_seq_len, dev)
+    ws = kv.decode_workspace(B, cfg.num_heads)
     outb = torch.empty_like(q)
     for _ in range(3):
         decode_attention(q, kv.k_cache[0], kv.v_cache[0], lens, None, outb, ws)

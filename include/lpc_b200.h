@@ -176,6 +176,37 @@ LPC_API int lpc_decode_attention(const void* q, const void* key_cache, const voi
                          int dtype, void* stream);
 
 /*
+ * Ragged KV layout (variable-length sequences packed back to back).
+ * Cache tensors are [kv_heads, total_rows, head_dim]; sequence b owns rows
+ * [seq_base[b], seq_base[b] + seq_cap[b]) of every head (seq_base int64 and
+ * seq_cap int32, device arrays of `batch` entries).  Memory then grows with the
+ * sum of the sequences' capacities instead of batch * max length -- what lets
+ * 64 prompts of 1k-8k tokens (+256 generated) fit one GPU.
+ * Replaces the dense per-layer cache of KVCacheManager (kv_manager.py:90-121)
+ * for mixed-length batches; the paged/ragged cache of runtime/paged_cache.py:14-57.
+ *
+ * lpc_rope_kv_append_ragged: as lpc_rope_kv_append, writing position p of
+ *   sequence b at row seq_base[b] + p; p >= seq_cap[b], or a row range outside
+ *   the buffer, is skipped and flagged in lpc_device_status().
+ * lpc_decode_attention_ragged: as lpc_decode_attention over keys
+ *   [0, seq_lens[b]) of sequence b's rows; max_seq_len bounds every seq_cap
+ *   (it sizes the split grid and the workspace, as in lpc_decode_attention).
+ */
+LPC_API int lpc_rope_kv_append_ragged(const void* qkv, const int64_t* positions, const void* cos,
+                                      const void* sin, int64_t table_rows, void* q_out,
+                                      void* key_cache, void* value_cache, const int64_t* seq_base,
+                                      const int32_t* seq_cap, int64_t batch, int64_t seq,
+                                      int num_heads, int num_kv_heads, int head_dim,
+                                      int64_t total_rows, int dtype, int table_dtype, void* stream);
+LPC_API int lpc_decode_attention_ragged(const void* q, const void* key_cache,
+                                        const void* value_cache, const int32_t* seq_lens,
+                                        const int64_t* seq_base, const int32_t* seq_cap, void* out,
+                                        void* workspace, int64_t workspace_bytes, int64_t batch,
+                                        int heads, int kv_heads, int head_dim, int64_t total_rows,
+                                        int64_t max_seq_len, float sm_scale, int dtype,
+                                        void* stream);
+
+/*
  * Decode attention that allocates nothing.  No counterpart in the reference:
  * it is an addition for callers that cannot allocate device memory when they
  * run attention -- a plugin whose host application owns all of HBM (e.g. a

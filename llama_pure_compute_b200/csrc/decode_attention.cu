@@ -91,13 +91,47 @@ struct RawRow<2> {
   __device__ __forceinline__ void load(const uint8_t* p) { w[0] = *reinterpret_cast<const uint32_t*>(p); }
 };
 
+// Where a sequence's cache rows live.
+//   dense  (base == nullptr): cache [max_batch, Hkv, Smax, D], row (b, h, p) =
+//          (b * Hkv + h) * Smax + p, capacity Smax;
+//   ragged: cache [Hkv, total_rows, D], sequence b owns rows
+//          [base[b], base[b] + cap[b]) of every head: row = h * total_rows + base[b] + p.
+// length() clamps L to the capacity and zeroes it for a slot range outside the
+// buffer, flagging either in the device status.
+struct KvRows {
+  const int64_t* base;
+  const int32_t* cap;
+  int64_t total_rows;
+  __device__ __forceinline__ int length(int64_t b, int kvh, int Hkv, int64_t Smax, int L,
+                                        int64_t* row0, bool report) const {
+    int64_t c = Smax;
+    if (base == nullptr) {
+      *row0 = (b * Hkv + kvh) * Smax;
+    } else {
+      const int64_t sb = __ldg(base + b);
+      c = __ldg(cap + b);
+      if (sb < 0 || c < 0 || c > Smax || sb + c > total_rows) {
+        if (report) atomicOr(&g_decode_status, LPC_DEV_ERR_BOUNDS);
+        *row0 = 0;
+        return 0;
+      }
+      *row0 = (int64_t)kvh * total_rows + sb;
+    }
+    if (L > c) {  // never read past this sequence's cache rows
+      if (report) atomicOr(&g_decode_status, LPC_DEV_ERR_BOUNDS);
+      L = (int)c;
+    }
+    return L;
+  }
+};
+
 template <typename T, int D, int G>
 __global__ void __launch_bounds__((NCWARPS + 1) * 32)
     decode_split_kernel(const T* __restrict__ q, const T* __restrict__ kc,
                         const T* __restrict__ vc, const int32_t* __restrict__ seq_lens,
                         T* __restrict__ out, float* __restrict__ part_o,
                         float* __restrict__ part_ml, int H, int Hkv, int64_t Smax,
-                        int max_splits, float scale_log2) {
+                        int max_splits, float scale_log2, KvRows rows) {
   constexpr int DPL = D / 32;                    // dims per lane
   constexpr int ROW_BYTES = D * (int)sizeof(T);
   constexpr int SLAB = TILE * ROW_BYTES;         // one K or V stage
@@ -111,11 +145,8 @@ __global__ void __launch_bounds__((NCWARPS + 1) * 32)
   const int split = blockIdx.x;
   const int kvh = blockIdx.y;
   const int64_t b = blockIdx.z;
-  int L = __ldg(seq_lens + b);
-  if (L > Smax) {  // never read past this sequence's cache rows
-    if (split == 0 && threadIdx.x == 0) atomicOr(&g_decode_status, LPC_DEV_ERR_BOUNDS);
-    L = (int)Smax;
-  }
+  int64_t row0;  // cache row of (b, kv head, position 0)
+  int L = rows.length(b, kvh, Hkv, Smax, __ldg(seq_lens + b), &row0, split == 0 && threadIdx.x == 0);
   const int start = split * CHUNK;
   if (start >= L) return;  // uniform for the whole CTA, before any barrier
   const int end = min(start + CHUNK, L);
@@ -134,7 +165,7 @@ __global__ void __launch_bounds__((NCWARPS + 1) * 32)
   }
   __syncthreads();
 
-  const int64_t head_base = ((b * Hkv + kvh) * Smax) * D;  // elements
+  const int64_t head_base = row0 * D;  // elements
   float m_run[G], l_run[G], acc[G][DPL];
 
   if (warp == NCWARPS) {
@@ -305,10 +336,12 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const float* __restri
                                                           const float* __restrict__ part_ml,
                                                           const int32_t* __restrict__ seq_lens,
                                                           T* __restrict__ out, int H,
-                                                          int max_splits, int64_t Smax) {
+                                                          int max_splits, int64_t Smax,
+                                                          KvRows rows) {
   const int64_t bh = blockIdx.x;
   const int64_t b = bh / H;
-  const int L = min((int64_t)__ldg(seq_lens + b), Smax);
+  int64_t row0;
+  const int L = rows.length(b, 0, 1, Smax, __ldg(seq_lens + b), &row0, false);
   const int d = threadIdx.x;
   if (L <= 0) {
     out[bh * D + d] = Num<T>::from_f(0.f);
@@ -333,7 +366,7 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const float* __restri
 template <typename T, int D, int G>
 int launch_g(const void* q, const void* kc, const void* vc, const int32_t* lens, void* out,
              float* po, float* pml, int64_t B, int H, int Hkv, int64_t Smax, int max_splits,
-             float scale_log2, cudaStream_t s) {
+             float scale_log2, const KvRows& rows, cudaStream_t s) {
   constexpr int SLAB = TILE * D * 2;
   const int smem = 2 * NSTAGE * SLAB + 2 * NSTAGE * 8 + NCWARPS * G * (D + 2) * 4;
   static std::atomic<uint64_t> mask{0};
@@ -342,22 +375,22 @@ int launch_g(const void* q, const void* kc, const void* vc, const int32_t* lens,
   dim3 grid((unsigned)max_splits, (unsigned)Hkv, (unsigned)B);
   decode_split_kernel<T, D, G><<<grid, (NCWARPS + 1) * 32, smem, s>>>(
       (const T*)q, (const T*)kc, (const T*)vc, lens, (T*)out, po, pml, H, Hkv, Smax, max_splits,
-      scale_log2);
+      scale_log2, rows);
   if ((rc = lpc::check_launch("decode_attention (split)"))) return rc;
   decode_combine_kernel<T, D><<<(unsigned)(B * H), D, 0, s>>>(po, pml, lens, (T*)out, H,
-                                                              max_splits, Smax);
+                                                              max_splits, Smax, rows);
   return lpc::check_launch("decode_attention (combine)");
 }
 
 template <typename T, int D>
 int launch_d(int G, const void* q, const void* kc, const void* vc, const int32_t* lens,
              void* out, float* po, float* pml, int64_t B, int H, int Hkv, int64_t Smax,
-             int max_splits, float sl2, cudaStream_t s) {
+             int max_splits, float sl2, const KvRows& r, cudaStream_t s) {
   switch (G) {
-    case 1: return launch_g<T, D, 1>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, sl2, s);
-    case 2: return launch_g<T, D, 2>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, sl2, s);
-    case 4: return launch_g<T, D, 4>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, sl2, s);
-    case 8: return launch_g<T, D, 8>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, sl2, s);
+    case 1: return launch_g<T, D, 1>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, sl2, r, s);
+    case 2: return launch_g<T, D, 2>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, sl2, r, s);
+    case 4: return launch_g<T, D, 4>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, sl2, r, s);
+    case 8: return launch_g<T, D, 8>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, sl2, r, s);
   }
   lpc::set_error("decode_attention: heads/kv_heads = %d not supported (1, 2, 4 or 8)", G);
   return LPC_ERR_UNSUPPORTED;
@@ -372,19 +405,13 @@ extern "C" int64_t lpc_decode_attention_workspace_bytes(int64_t batch, int heads
   return batch * heads * max_splits * (int64_t)(head_dim + 2) * 4;
 }
 
-extern "C" int lpc_decode_attention(const void* q, const void* key_cache, const void* value_cache,
-                                    const int32_t* seq_lens, void* out, void* workspace,
-                                    int64_t workspace_bytes, int64_t batch, int heads,
-                                    int kv_heads, int head_dim, int64_t max_batch,
-                                    int64_t max_seq_len, float sm_scale, int dtype,
-                                    void* stream) {
+namespace {
+
+int decode_common(const void* q, const void* key_cache, const void* value_cache,
+                  const int32_t* seq_lens, void* out, void* workspace, int64_t workspace_bytes,
+                  int64_t batch, int heads, int kv_heads, int head_dim, int64_t max_seq_len,
+                  float sm_scale, int dtype, const KvRows& rows, void* stream) {
   using namespace lpc;
-  if (batch < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || max_batch <= 0 ||
-      max_seq_len <= 0 || batch > max_batch) {
-    set_error("decode_attention: invalid sizes (batch=%lld heads=%d kv_heads=%d max_batch=%lld)",
-              (long long)batch, heads, kv_heads, (long long)max_batch);
-    return LPC_ERR_INVALID;
-  }
   if (batch == 0) return LPC_OK;
   if (dtype != LPC_DTYPE_BF16 && dtype != LPC_DTYPE_F16) {
     set_error("decode_attention: only bf16 and fp16 are supported");
@@ -418,14 +445,59 @@ extern "C" int lpc_decode_attention(const void* q, const void* key_cache, const 
   const float sl2 = sm_scale * LOG2E;
   const int G = heads / kv_heads;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int ms = (int)max_splits;
   if (dtype == LPC_DTYPE_BF16) {
     if (head_dim == 128)
-      return launch_d<__nv_bfloat16, 128>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, (int)max_splits, sl2, s);
-    return launch_d<__nv_bfloat16, 64>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, (int)max_splits, sl2, s);
+      return launch_d<__nv_bfloat16, 128>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
+    return launch_d<__nv_bfloat16, 64>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
   }
   if (head_dim == 128)
-    return launch_d<__half, 128>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, (int)max_splits, sl2, s);
-  return launch_d<__half, 64>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, (int)max_splits, sl2, s);
+    return launch_d<__half, 128>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
+  return launch_d<__half, 64>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
+}
+
+}  // namespace
+
+extern "C" int lpc_decode_attention(const void* q, const void* key_cache, const void* value_cache,
+                                    const int32_t* seq_lens, void* out, void* workspace,
+                                    int64_t workspace_bytes, int64_t batch, int heads,
+                                    int kv_heads, int head_dim, int64_t max_batch,
+                                    int64_t max_seq_len, float sm_scale, int dtype,
+                                    void* stream) {
+  using namespace lpc;
+  if (batch < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || max_batch <= 0 ||
+      max_seq_len <= 0 || batch > max_batch) {
+    set_error("decode_attention: invalid sizes (batch=%lld heads=%d kv_heads=%d max_batch=%lld)",
+              (long long)batch, heads, kv_heads, (long long)max_batch);
+    return LPC_ERR_INVALID;
+  }
+  const KvRows dense{nullptr, nullptr, 0};
+  return decode_common(q, key_cache, value_cache, seq_lens, out, workspace, workspace_bytes, batch,
+                       heads, kv_heads, head_dim, max_seq_len, sm_scale, dtype, dense, stream);
+}
+
+extern "C" int lpc_decode_attention_ragged(const void* q, const void* key_cache,
+                                           const void* value_cache, const int32_t* seq_lens,
+                                           const int64_t* seq_base, const int32_t* seq_cap,
+                                           void* out, void* workspace, int64_t workspace_bytes,
+                                           int64_t batch, int heads, int kv_heads, int head_dim,
+                                           int64_t total_rows, int64_t max_seq_len,
+                                           float sm_scale, int dtype, void* stream) {
+  using namespace lpc;
+  if (batch < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || total_rows <= 0 ||
+      max_seq_len <= 0) {
+    set_error("decode_attention_ragged: invalid sizes (batch=%lld heads=%d kv_heads=%d "
+              "total_rows=%lld max_seq_len=%lld)", (long long)batch, heads, kv_heads,
+              (long long)total_rows, (long long)max_seq_len);
+    return LPC_ERR_INVALID;
+  }
+  if (batch > 0 && (!seq_base || !seq_cap)) {
+    set_error("decode_attention_ragged: seq_base and seq_cap are required");
+    return LPC_ERR_INVALID;
+  }
+  const KvRows ragged{seq_base, seq_cap, total_rows};
+  return decode_common(q, key_cache, value_cache, seq_lens, out, workspace, workspace_bytes, batch,
+                       heads, kv_heads, head_dim, max_seq_len, sm_scale, dtype, ragged, stream);
 }
 
 // ---------------------------------------------------------------------------

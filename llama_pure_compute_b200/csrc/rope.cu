@@ -156,7 +156,8 @@ __global__ void __launch_bounds__(256) rope_kv_append_kernel(
     const T* __restrict__ qkv, const int64_t* __restrict__ positions, const TT* __restrict__ cosb,
     const TT* __restrict__ sinb, int64_t table_rows, T* __restrict__ q_out,
     T* __restrict__ kcache, T* __restrict__ vcache, int64_t batch, int64_t seq, int num_heads,
-    int num_kv_heads, int head_dim, int64_t max_batch, int64_t max_seq_len) {
+    int num_kv_heads, int head_dim, int64_t max_batch, int64_t max_seq_len,
+    const int64_t* __restrict__ seq_base, const int32_t* __restrict__ seq_cap, int64_t total_rows) {
   const int half = head_dim >> 1;
   const int chunks = half / VEC;
   const int heads_all = num_heads + 2 * num_kv_heads;
@@ -171,7 +172,23 @@ __global__ void __launch_bounds__(256) rope_kv_append_kernel(
   const int64_t s = tok - b * seq;
   const int64_t pos = __ldg(positions + tok);
   if (pos < 0) return;
-  if (pos >= max_seq_len || pos >= table_rows || b >= max_batch) {
+  // cache row of (b, kv head 0, pos) and the distance between kv heads:
+  //   dense  [max_batch, Hkv, max_seq_len, D]: (b * Hkv) * max_seq_len + pos, max_seq_len
+  //   ragged [Hkv, total_rows, D] (seq_base != nullptr): seq_base[b] + pos, total_rows
+  int64_t row, head_rows;
+  bool ok;
+  if (seq_base == nullptr) {
+    ok = pos < max_seq_len && b < max_batch;
+    row = b * num_kv_heads * max_seq_len + pos;
+    head_rows = max_seq_len;
+  } else {
+    const int64_t sb = __ldg(seq_base + b);
+    const int64_t cap = __ldg(seq_cap + b);
+    ok = sb >= 0 && pos < cap && sb + cap <= total_rows;
+    row = sb + pos;
+    head_rows = total_rows;
+  }
+  if (!ok || pos >= table_rows) {
     atomicOr(&g_rope_status, LPC_DEV_ERR_BOUNDS);
     return;
   }
@@ -183,7 +200,7 @@ __global__ void __launch_bounds__(256) rope_kv_append_kernel(
 
   if (hh >= num_heads + num_kv_heads) {  // V: plain copy into the cache
     const int h = hh - num_heads - num_kv_heads;
-    T* dst = vcache + ((b * num_kv_heads + h) * max_seq_len + pos) * (int64_t)head_dim;
+    T* dst = vcache + (row + h * head_rows) * (int64_t)head_dim;
     store_f<T, VEC>(dst + d, x0);
     store_f<T, VEC>(dst + d + half, x1);
     return;
@@ -202,7 +219,7 @@ __global__ void __launch_bounds__(256) rope_kv_append_kernel(
     dst = q_out + ((b * num_heads + hh) * seq + s) * (int64_t)head_dim;
   } else {
     const int h = hh - num_heads;
-    dst = kcache + ((b * num_kv_heads + h) * max_seq_len + pos) * (int64_t)head_dim;
+    dst = kcache + (row + h * head_rows) * (int64_t)head_dim;
   }
   store_f<T, VEC>(dst + d, o0);
   store_f<T, VEC>(dst + d + half, o1);
@@ -245,13 +262,14 @@ int launch_rope_t(int table_dtype, void* q, void* k, const void* c, const void* 
 template <typename T, typename TT>
 int launch_fused(const void* qkv, const int64_t* positions, const void* c, const void* sn,
                  int64_t rows, void* q_out, void* kc, void* vc, int64_t batch, int64_t seq, int h,
-                 int hkv, int d, int64_t max_batch, int64_t max_seq, cudaStream_t s) {
+                 int hkv, int d, int64_t max_batch, int64_t max_seq, const int64_t* seq_base,
+                 const int32_t* seq_cap, int64_t total_rows, cudaStream_t s) {
   constexpr int VEC = 16 / (int)sizeof(T);
   const int threads = 256;
   const int64_t work = batch * seq * (h + 2 * hkv) * (d / 2 / VEC);
   rope_kv_append_kernel<T, TT, VEC><<<(unsigned)((work + threads - 1) / threads), threads, 0, s>>>(
       (const T*)qkv, positions, (const TT*)c, (const TT*)sn, rows, (T*)q_out, (T*)kc, (T*)vc, batch,
-      seq, h, hkv, d, max_batch, max_seq);
+      seq, h, hkv, d, max_batch, max_seq, seq_base, seq_cap, total_rows);
   return lpc::check_launch("rope_kv_append");
 }
 
@@ -297,24 +315,15 @@ extern "C" int lpc_rope_forward(void* q, void* k, const void* cos, const void* s
   return LPC_ERR_UNSUPPORTED;
 }
 
-extern "C" int lpc_rope_kv_append(const void* qkv, const int64_t* positions, const void* cos,
-                                  const void* sin, int64_t table_rows, void* q_out,
-                                  void* key_cache, void* value_cache, int64_t batch, int64_t seq,
-                                  int num_heads, int num_kv_heads, int head_dim,
-                                  int64_t max_batch, int64_t max_seq_len, int dtype,
-                                  int table_dtype, void* stream) {
+namespace {
+
+int rope_kv_append_common(const void* qkv, const int64_t* positions, const void* cos,
+                          const void* sin, int64_t table_rows, void* q_out, void* key_cache,
+                          void* value_cache, int64_t batch, int64_t seq, int num_heads,
+                          int num_kv_heads, int head_dim, int64_t max_batch, int64_t max_seq_len,
+                          const int64_t* seq_base, const int32_t* seq_cap, int64_t total_rows,
+                          int dtype, int table_dtype, void* stream) {
   using namespace lpc;
-  if (batch < 0 || seq < 0 || num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 ||
-      max_batch <= 0 || max_seq_len <= 0 || table_rows <= 0) {
-    set_error("rope_kv_append: invalid sizes");
-    return LPC_ERR_INVALID;
-  }
-  if (batch == 0 || seq == 0) return LPC_OK;
-  if (batch > max_batch) {
-    set_error("rope_kv_append: batch %lld exceeds cache capacity %lld", (long long)batch,
-              (long long)max_batch);
-    return LPC_ERR_INVALID;
-  }
   if (!qkv || !positions || !cos || !sin || !q_out || !key_cache || !value_cache) {
     set_error("rope_kv_append: null pointer");
     return LPC_ERR_INVALID;
@@ -333,17 +342,66 @@ extern "C" int lpc_rope_kv_append(const void* qkv, const int64_t* positions, con
     return LPC_ERR_UNSUPPORTED;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define LPC_FUSED(T, TT)                                                                        \
+  return launch_fused<T, TT>(qkv, positions, cos, sin, table_rows, q_out, key_cache, value_cache, \
+                             batch, seq, num_heads, num_kv_heads, head_dim, max_batch,           \
+                             max_seq_len, seq_base, seq_cap, total_rows, s)
   if (dtype == LPC_DTYPE_BF16) {
-    if (table_dtype == LPC_DTYPE_BF16)
-      return launch_fused<__nv_bfloat16, __nv_bfloat16>(qkv, positions, cos, sin, table_rows, q_out, key_cache, value_cache, batch, seq, num_heads, num_kv_heads, head_dim, max_batch, max_seq_len, s);
-    if (table_dtype == LPC_DTYPE_F32)
-      return launch_fused<__nv_bfloat16, float>(qkv, positions, cos, sin, table_rows, q_out, key_cache, value_cache, batch, seq, num_heads, num_kv_heads, head_dim, max_batch, max_seq_len, s);
+    if (table_dtype == LPC_DTYPE_BF16) LPC_FUSED(__nv_bfloat16, __nv_bfloat16);
+    if (table_dtype == LPC_DTYPE_F32) LPC_FUSED(__nv_bfloat16, float);
   } else {
-    if (table_dtype == LPC_DTYPE_F16)
-      return launch_fused<__half, __half>(qkv, positions, cos, sin, table_rows, q_out, key_cache, value_cache, batch, seq, num_heads, num_kv_heads, head_dim, max_batch, max_seq_len, s);
-    if (table_dtype == LPC_DTYPE_F32)
-      return launch_fused<__half, float>(qkv, positions, cos, sin, table_rows, q_out, key_cache, value_cache, batch, seq, num_heads, num_kv_heads, head_dim, max_batch, max_seq_len, s);
+    if (table_dtype == LPC_DTYPE_F16) LPC_FUSED(__half, __half);
+    if (table_dtype == LPC_DTYPE_F32) LPC_FUSED(__half, float);
   }
+#undef LPC_FUSED
   set_error("rope_kv_append: table dtype must match activations or be fp32");
   return LPC_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+
+extern "C" int lpc_rope_kv_append(const void* qkv, const int64_t* positions, const void* cos,
+                                  const void* sin, int64_t table_rows, void* q_out,
+                                  void* key_cache, void* value_cache, int64_t batch, int64_t seq,
+                                  int num_heads, int num_kv_heads, int head_dim,
+                                  int64_t max_batch, int64_t max_seq_len, int dtype,
+                                  int table_dtype, void* stream) {
+  using namespace lpc;
+  if (batch < 0 || seq < 0 || num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 ||
+      max_batch <= 0 || max_seq_len <= 0 || table_rows <= 0) {
+    set_error("rope_kv_append: invalid sizes");
+    return LPC_ERR_INVALID;
+  }
+  if (batch == 0 || seq == 0) return LPC_OK;
+  if (batch > max_batch) {
+    set_error("rope_kv_append: batch %lld exceeds cache capacity %lld", (long long)batch,
+              (long long)max_batch);
+    return LPC_ERR_INVALID;
+  }
+  return rope_kv_append_common(qkv, positions, cos, sin, table_rows, q_out, key_cache, value_cache,
+                               batch, seq, num_heads, num_kv_heads, head_dim, max_batch,
+                               max_seq_len, nullptr, nullptr, 0, dtype, table_dtype, stream);
+}
+
+extern "C" int lpc_rope_kv_append_ragged(const void* qkv, const int64_t* positions,
+                                         const void* cos, const void* sin, int64_t table_rows,
+                                         void* q_out, void* key_cache, void* value_cache,
+                                         const int64_t* seq_base, const int32_t* seq_cap,
+                                         int64_t batch, int64_t seq, int num_heads,
+                                         int num_kv_heads, int head_dim, int64_t total_rows,
+                                         int dtype, int table_dtype, void* stream) {
+  using namespace lpc;
+  if (batch < 0 || seq < 0 || num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 ||
+      total_rows <= 0 || table_rows <= 0) {
+    set_error("rope_kv_append_ragged: invalid sizes");
+    return LPC_ERR_INVALID;
+  }
+  if (batch == 0 || seq == 0) return LPC_OK;
+  if (!seq_base || !seq_cap) {
+    set_error("rope_kv_append_ragged: seq_base and seq_cap are required");
+    return LPC_ERR_INVALID;
+  }
+  return rope_kv_append_common(qkv, positions, cos, sin, table_rows, q_out, key_cache, value_cache,
+                               batch, seq, num_heads, num_kv_heads, head_dim, batch, 1, seq_base,
+                               seq_cap, total_rows, dtype, table_dtype, stream);
 }

@@ -20,6 +20,7 @@ import torch.nn.functional as F
 
 from .config import LlamaModelConfig
 from .kv_manager import KVCacheManager
+from .ragged_cache import RaggedKVCache
 
 __all__ = ["GenerationConfig", "apply_repetition_penalty", "sample_next_token", "LlamaGenerator",
            "BatchedGreedyDecoder"]
@@ -83,6 +84,7 @@ class _RowView:
         self.max_seq_len = base.max_seq_len
         self.max_batch_size = count
         self.n_kv_heads = base.n_kv_heads
+        self.head_dim = base.head_dim
         self.num_layers = base.num_layers
 
     def append_qkv(self, **kw):
@@ -90,6 +92,15 @@ class _RowView:
 
     def set_seq_lens(self, positions):
         return KVCacheManager.set_seq_lens(self, positions)  # type: ignore[arg-type]
+
+    def decode_workspace(self, batch, num_heads):
+        return KVCacheManager.decode_workspace(self, batch, num_heads)  # type: ignore[arg-type]
+
+    def prepare_forward(self, positions, ctx, num_heads):
+        return KVCacheManager.prepare_forward(self, positions, ctx, num_heads)  # type: ignore[arg-type]
+
+    def attend(self, **kw):
+        return KVCacheManager.attend(self, **kw)  # type: ignore[arg-type]
 
     def _check_layer(self, layer_idx: int) -> None:
         if not 0 <= layer_idx < self.num_layers:
@@ -158,10 +169,12 @@ class BatchedGreedyDecoder:
     generated tokens; ``step`` advances every sequence by one token.
     """
 
-    def __init__(self, model: torch.nn.Module, kv_cache: KVCacheManager, batch_size: int,
-                 use_cuda_graph: bool = True, prefill_chunk: int = 16) -> None:
-        if batch_size > kv_cache.max_batch_size:
-            raise ValueError("batch_size exceeds the cache's max_batch_size")
+    def __init__(self, model: torch.nn.Module, kv_cache: Union[KVCacheManager, RaggedKVCache],
+                 batch_size: int, use_cuda_graph: bool = True, prefill_chunk: int = 16) -> None:
+        self.ragged = isinstance(kv_cache, RaggedKVCache)
+        cap = kv_cache.num_sequences if self.ragged else kv_cache.max_batch_size
+        if batch_size > cap:
+            raise ValueError("batch_size exceeds the cache's capacity")
         self.model = model
         self.kv = kv_cache
         self.B = batch_size
@@ -177,7 +190,8 @@ class BatchedGreedyDecoder:
     @torch.inference_mode()
     def prefill(self, prompts: Union[torch.Tensor, List[List[int]]]) -> torch.Tensor:
         """Returns the first generated token of each sequence (device, [B])."""
-        self.kv.begin_request(self.B)
+        if not self.ragged:
+            self.kv.begin_request(self.B)
         if isinstance(prompts, torch.Tensor):
             rows = [prompts[i] for i in range(prompts.shape[0])]
         else:
@@ -185,7 +199,8 @@ class BatchedGreedyDecoder:
         if len(rows) != self.B:
             raise ValueError("one prompt per sequence is required")
         lens = [int(r.numel()) for r in rows]
-        if max(lens) >= self.kv.max_seq_len:
+        caps = self.kv.capacities[:self.B] if self.ragged else [self.kv.max_seq_len] * self.B
+        if any(n >= c for n, c in zip(lens, caps)):
             raise ValueError("prompt does not fit the cache")
         first = torch.empty(self.B, dtype=torch.long, device=self.device)
         i = 0
@@ -196,10 +211,16 @@ class BatchedGreedyDecoder:
             ids = torch.stack([r.to(self.device) for r in rows[i:j]])
             P = lens[i]
             pos = torch.arange(P, device=self.device, dtype=torch.long).unsqueeze(0).expand(j - i, -1)
-            view = _RowView(self.kv, i, j - i)
+            if self.ragged:
+                self.kv.select(range(i, j))
+                view = self.kv
+            else:
+                view = _RowView(self.kv, i, j - i)
             logits = self.model(ids, positions=pos, kv_cache=view, last_token_only=True)
             first[i:j] = torch.argmax(logits[:, -1, :], dim=-1)
             i = j
+        if self.ragged:
+            self.kv.select(range(self.B))  # decode steps run on every sequence
         self.positions[:, 0] = torch.tensor(lens, dtype=torch.long, device=self.device)
         self.tokens[:, 0] = first
         return first

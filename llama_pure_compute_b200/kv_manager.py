@@ -11,7 +11,9 @@ per layer, allocated once in HBM):
     at arbitrary per-sequence positions (ragged batches);
   * ``set_seq_lens`` -- per-sequence context lengths kept on the device
     (``seq_lens`` int32 [max_batch]), consumed by the ragged decode kernel
-    without a host sync.
+    without a host sync;
+  * ``prepare_forward`` / ``attend`` -- the step interface the model calls
+    (shared with ``ragged_cache.RaggedKVCache``).
 """
 from __future__ import annotations
 
@@ -21,7 +23,8 @@ from typing import Tuple, Union
 
 import torch
 
-from .ops import rope_kv_append, update_kv_cache
+from .flash_attention import flash_attention_v2
+from .ops import decode_attention, decode_attention_workspace, rope_kv_append, update_kv_cache
 
 logger = logging.getLogger("llama_pure_compute_b200.kv_manager")
 
@@ -208,3 +211,49 @@ class KVCacheManager:
             raise ValueError("batch size exceeds cache capacity")
         self.seq_lens[:b].copy_(positions[:, -1] + 1)
         return self.seq_lens[:b]
+
+    # -- model-facing step interface (KVCacheManager and RaggedKVCache) -------
+    def decode_workspace(self, batch: int, num_heads: int) -> torch.Tensor:
+        """Split-KV partials buffer of the decode kernel, kept across steps."""
+        key = (batch, num_heads)
+        ws = getattr(self, "_decode_ws", None)
+        if ws is None or ws[0] != key:
+            t = decode_attention_workspace(batch, num_heads, self.max_seq_len, self.head_dim,
+                                           self.seq_lens.device)
+            ws = (key, t)
+            self._decode_ws = ws
+        return ws[1]
+
+    @torch.no_grad()
+    def prepare_forward(self, positions: torch.Tensor, ctx, num_heads: int) -> None:
+        """Per-forward state: a one-token step is a decode step (device
+        seq_lens, no host sync); longer inputs are a prefill starting at
+        positions[0, 0] for every row (one host read per forward, where the
+        reference reads it in every layer, model.py:159-161)."""
+        B, S = positions.shape
+        if S == 1:
+            ctx.decode = True
+            ctx.seq_lens = self.set_seq_lens(positions)
+            ctx.workspace = self.decode_workspace(B, num_heads)
+        else:
+            ctx.decode = False
+            ctx.start_pos = int(positions[0, 0].item())
+            self.seq_lens[:B] = ctx.start_pos + S
+
+    def attend(self, *, layer_idx: int, qkv: torch.Tensor, positions: torch.Tensor, ctx,
+               num_heads: int, scale: float) -> torch.Tensor:
+        """RoPE + append of ``qkv`` [B, S, (H+2Hkv)*D], then causal attention of
+        the new queries over the cached context; returns [B, S, H*D]."""
+        B, S, _ = qkv.shape
+        D = self.head_dim
+        q = self.append_qkv(layer_idx=layer_idx, qkv=qkv, positions=positions,
+                            cos_table=ctx.cos_table, sin_table=ctx.sin_table, num_heads=num_heads)
+        kc, vc = self.k_cache[layer_idx], self.v_cache[layer_idx]
+        if ctx.decode:
+            out = decode_attention(q.view(B, num_heads, D), kc, vc, ctx.seq_lens, scale,
+                                   workspace=ctx.workspace)
+            return out.view(B, 1, num_heads * D)
+        end = ctx.start_pos + S
+        out = flash_attention_v2(q, kc[:B, :, :end, :], vc[:B, :, :end, :], causal=True,
+                                 sm_scale=scale)
+        return out.transpose(1, 2).reshape(B, S, num_heads * D)

@@ -36,7 +36,7 @@ import torch.nn.functional as F
 from .config import LlamaModelConfig
 from .flash_attention import flash_attention_v2
 from .kv_manager import KVCacheManager
-from .ops import decode_attention, rmsswiglu_forward, rope_forward
+from .ops import rmsswiglu_forward, rope_forward
 from .rmsnorm import RMSNorm
 
 # Decode steps with at most this many tokens run the SwiGLU GEMM on packed
@@ -131,18 +131,9 @@ class LlamaAttention(nn.Module):
         if kv_cache is not None:
             if ctx is None or ctx.cos_table is None:
                 raise ValueError("cached attention needs the model's RoPE tables (call via LlamaModel)")
-            q = kv_cache.append_qkv(layer_idx=layer_idx, qkv=qkv, positions=positions,
-                                    cos_table=ctx.cos_table, sin_table=ctx.sin_table, num_heads=H)
-            kc, vc = kv_cache.k_cache[layer_idx], kv_cache.v_cache[layer_idx]
-            if ctx.decode:
-                out = decode_attention(q.view(B, H, D), kc, vc, ctx.seq_lens, self.scale,
-                                       workspace=ctx.workspace)
-                out = out.view(B, 1, H * D)
-            else:
-                end = ctx.start_pos + S
-                out = flash_attention_v2(q, kc[:B, :, :end, :], vc[:B, :, :end, :], causal=True,
-                                         sm_scale=self.scale)
-                out = out.transpose(1, 2).reshape(B, S, H * D)
+            # RoPE + append + attention over the cache (dense or ragged layout)
+            out = kv_cache.attend(layer_idx=layer_idx, qkv=qkv, positions=positions, ctx=ctx,
+                                  num_heads=H, scale=self.scale)
         else:
             q = qkv[..., : H * D].reshape(B, S, H, D)
             k = qkv[..., H * D:(H + Hkv) * D].reshape(B, S, Hkv, D)
@@ -231,7 +222,6 @@ class LlamaModel(nn.Module):
         cos, sin = precompute_freqs_cis(config.head_dim, config.max_seq_len, theta=config.rope_theta)
         self.register_buffer("cos_cached", cos, persistent=False)
         self.register_buffer("sin_cached", sin, persistent=False)
-        self._decode_ws: Dict[tuple, torch.Tensor] = {}
 
     def reset_rope_tables(self) -> None:
         """Recompute cos/sin (e.g. after materialising a meta-device model)."""
@@ -241,16 +231,6 @@ class LlamaModel(nn.Module):
         dt = self.embed_tokens.weight.dtype
         self.cos_cached = cos.to(dt)
         self.sin_cached = sin.to(dt)
-
-    def _workspace(self, batch: int, max_seq_len: int, device) -> torch.Tensor:
-        from .ops import decode_attention_workspace
-        key = (batch, max_seq_len, str(device))
-        ws = self._decode_ws.get(key)
-        if ws is None:
-            ws = decode_attention_workspace(batch, self.config.num_heads, max_seq_len,
-                                            self.config.head_dim, device)
-            self._decode_ws = {key: ws}
-        return ws
 
     def forward(
         self,
@@ -267,14 +247,7 @@ class LlamaModel(nn.Module):
         cos = sin = None
         if kv_cache is not None:
             ctx.cos_table, ctx.sin_table = self.cos_cached, self.sin_cached
-            if S == 1:
-                ctx.decode = True
-                ctx.seq_lens = kv_cache.set_seq_lens(positions)
-                ctx.workspace = self._workspace(B, kv_cache.max_seq_len, h.device)
-            else:
-                # one host read per forward (the reference reads it in every layer)
-                ctx.start_pos = int(positions[0, 0].item())
-                kv_cache.seq_lens[:B] = ctx.start_pos + S
+            kv_cache.prepare_forward(positions, ctx, self.config.num_heads)
         else:
             cos = self.cos_cached[positions]
             sin = self.sin_cached[positions]

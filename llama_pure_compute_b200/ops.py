@@ -30,6 +30,8 @@ __all__ = [
     "rmsnorm_forward",
     "rope_kv_append",
     "decode_attention",
+    "rope_kv_append_ragged",
+    "decode_attention_ragged",
 ]
 
 
@@ -333,4 +335,111 @@ def decode_attention(
         float(sm_scale), _lib.dtype_code(q.dtype, "decode_attention"), _lib.stream_of(q))
     _lib.check(rc, "decode_attention")
     _lib.count_launch("lpc_decode_attention")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Ragged KV layout: caches [Hkv, total_rows, D], sequence b owns rows
+# [seq_base[b], seq_base[b] + seq_cap[b]) of every head.
+# ---------------------------------------------------------------------------
+def _check_ragged_index(seq_base: torch.Tensor, seq_cap: torch.Tensor, B: int) -> None:
+    _require_cuda(seq_base, "seq_base")
+    _require_cuda(seq_cap, "seq_cap")
+    if seq_base.dtype != torch.int64 or seq_cap.dtype != torch.int32:
+        raise TypeError("LlamaPureComputeError: seq_base must be int64 and seq_cap int32.")
+    if seq_base.numel() < B or seq_cap.numel() < B or not seq_base.is_contiguous() \
+            or not seq_cap.is_contiguous():
+        raise ValueError("LlamaPureComputeError: seq_base/seq_cap need a contiguous entry per sequence.")
+
+
+def rope_kv_append_ragged(
+    qkv: torch.Tensor,
+    positions: torch.Tensor,
+    cos_table: torch.Tensor,
+    sin_table: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    seq_base: torch.Tensor,
+    seq_cap: torch.Tensor,
+    num_heads: int,
+    num_kv_heads: int,
+    q_out: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """``rope_kv_append`` into a ragged cache ``[Hkv, total_rows, D]``: row b of
+    ``qkv`` [B, S, (H+2Hkv)*D] is sequence b, its position p goes to cache row
+    ``seq_base[b] + p``.  Returns q as [B, H, S, D]."""
+    for t, n in ((qkv, "qkv"), (positions, "positions"), (cos_table, "cos"), (sin_table, "sin"),
+                 (key_cache, "key_cache"), (value_cache, "value_cache")):
+        _require_cuda(t, n)
+    B, S, W = qkv.shape
+    Hkv, total_rows, D = key_cache.shape
+    if Hkv != num_kv_heads or W != (num_heads + 2 * num_kv_heads) * D:
+        raise ValueError("LlamaPureComputeError: qkv width does not match heads * head_dim.")
+    if value_cache.shape != key_cache.shape:
+        raise ValueError("LlamaPureComputeError: key and value caches differ in shape.")
+    if cos_table.shape[-1] != D or cos_table.dim() != 2:
+        raise ValueError("LlamaPureComputeError: rope tables must be [max_pos, head_dim].")
+    _check_ragged_index(seq_base, seq_cap, B)
+    qkv = qkv.contiguous()
+    pos = positions.to(torch.int64).contiguous()
+    if pos.shape != (B, S):
+        raise ValueError("LlamaPureComputeError: positions must be [batch, seq].")
+    if q_out is None:
+        q_out = torch.empty(B, num_heads, S, D, dtype=qkv.dtype, device=qkv.device)
+    rc = _lib.load().lpc_rope_kv_append_ragged(
+        qkv.data_ptr(), pos.data_ptr(), cos_table.data_ptr(), sin_table.data_ptr(),
+        cos_table.shape[0], q_out.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
+        seq_base.data_ptr(), seq_cap.data_ptr(), B, S, num_heads, num_kv_heads, D, total_rows,
+        _lib.dtype_code(qkv.dtype, "rope_kv_append_ragged"),
+        _lib.dtype_code(cos_table.dtype, "rope_kv_append_ragged"), _lib.stream_of(qkv))
+    _lib.check(rc, "rope_kv_append_ragged")
+    _lib.count_launch("lpc_rope_kv_append_ragged")
+    return q_out
+
+
+def decode_attention_ragged(
+    q: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    seq_lens: torch.Tensor,
+    seq_base: torch.Tensor,
+    seq_cap: torch.Tensor,
+    max_seq_len: int,
+    sm_scale: Optional[float] = None,
+    out: Optional[torch.Tensor] = None,
+    workspace: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """``decode_attention`` over a ragged cache ``[Hkv, total_rows, D]``:
+    sequence b attends to rows ``seq_base[b] .. seq_base[b] + seq_lens[b]``.
+    ``max_seq_len`` must bound every ``seq_cap`` entry."""
+    for t, n in ((q, "q"), (key_cache, "key_cache"), (value_cache, "value_cache"),
+                 (seq_lens, "seq_lens")):
+        _require_cuda(t, n)
+    if seq_lens.dtype != torch.int32:
+        raise TypeError("LlamaPureComputeError: seq_lens must be int32.")
+    Hkv, total_rows, D = key_cache.shape
+    B, H = q.shape[0], q.shape[1]
+    if q.shape[-1] != D or q.numel() != B * H * D:
+        raise ValueError("LlamaPureComputeError: q must be [B, H, D] with the cache's head_dim.")
+    if seq_lens.numel() < B:
+        raise ValueError("LlamaPureComputeError: seq_lens must have an entry per sequence.")
+    if q.dtype != key_cache.dtype:
+        raise TypeError("LlamaPureComputeError: q and cache dtypes differ.")
+    _check_ragged_index(seq_base, seq_cap, B)
+    qc = q.contiguous()
+    if sm_scale is None:
+        sm_scale = D ** -0.5
+    if out is None:
+        out = torch.empty_like(qc)
+    lib = _lib.load()
+    need = lib.lpc_decode_attention_workspace_bytes(B, H, max_seq_len, D)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=q.device)
+    rc = lib.lpc_decode_attention_ragged(
+        qc.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), seq_lens.data_ptr(),
+        seq_base.data_ptr(), seq_cap.data_ptr(), out.data_ptr(), workspace.data_ptr(),
+        workspace.numel(), B, H, Hkv, D, total_rows, max_seq_len, float(sm_scale),
+        _lib.dtype_code(q.dtype, "decode_attention_ragged"), _lib.stream_of(q))
+    _lib.check(rc, "decode_attention_ragged")
+    _lib.count_launch("lpc_decode_attention_ragged")
     return out
