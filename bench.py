@@ -65,8 +65,9 @@ def parse():
                     help="untimed decode steps before the timed ones (default: enough to centre "
                          "the timed steps on the mean context)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--suite", choices=["decode", "ops"], default="decode",
-                    help="decode: the 7B decode workload (default); ops: per-op roofline lines")
+    ap.add_argument("--suite", choices=["decode", "ops", "longctx"], default="decode",
+                    help="decode: the 7B decode workload (default); ops: per-op roofline lines; "
+                         "longctx: 64 prompts of 1k-8k tokens, prefill + 256 decode steps")
     ap.add_argument("--only", default="", help="comma list of op lines for --suite ops")
     ap.add_argument("--decode-batch", type=int, default=64,
                     help="sequences of the ragged decode op line (64 = the decode op shape)")
@@ -607,10 +608,132 @@ def run_ops(args):
     return out
 
 
+# ---------------------------------------------------------------------------
+# long-context mixed run (--suite longctx)
+# ---------------------------------------------------------------------------
+LONG_SEQS, LONG_MIN, LONG_MAX, LONG_NEW, LONG_SEED = 64, 1024, 8192, 256, 4
+KV_BYTES_PER_TOKEN_7B = 32 * 2 * 32 * 128 * 2   # 32 layers x (K, V) x 32 heads x 128 x bf16
+WEIGHT_BYTES_7B = 13.215e9                      # all layers + lm_head, bf16
+
+
+def long_prompts():
+    """64 prompts of 1024..8192 tokens (uniform), ids uniform over the vocabulary."""
+    g = torch.Generator().manual_seed(LONG_SEED)
+    lens = torch.randint(LONG_MIN, LONG_MAX + 1, (LONG_SEQS,), generator=g).tolist()
+    return [torch.randint(0, 32000, (n,), generator=g).tolist() for n in lens]
+
+
+def lpt_partition(weights, world):
+    """Longest-processing-time-first: heaviest sequence to the least-loaded rank."""
+    loads = [0] * world
+    parts = [[] for _ in range(world)]
+    for i in sorted(range(len(weights)), key=lambda i: (-weights[i], i)):
+        r = min(range(world), key=lambda r: (loads[r], r))
+        parts[r].append(i)
+        loads[r] += weights[i]
+    return [sorted(p) for p in parts], loads
+
+
+def run_longctx(args, world, rank, local):
+    from llama_pure_compute_b200 import _lib
+    from llama_pure_compute_b200.generate import BatchedGreedyDecoder
+    from llama_pure_compute_b200.model import LlamaForCausalLM
+    from llama_pure_compute_b200.ragged_cache import RaggedKVCache
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    _lib.load()
+    prompts = long_prompts()
+    lens = [len(p) for p in prompts]
+    parts, loads = lpt_partition([n + LONG_NEW for n in lens], world)
+    mine = parts[rank]
+    cfg = model_config(args.layers, LONG_MAX + LONG_NEW)
+    model = LlamaForCausalLM.random_init(cfg, device=dev, dtype=torch.bfloat16, seed=SEED)
+    cache = RaggedKVCache(num_layers=cfg.num_layers, capacities=[lens[i] + LONG_NEW for i in mine],
+                          n_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim,
+                          dtype=torch.bfloat16, device=dev)
+    free, _ = torch.cuda.mem_get_info(dev)
+    # the packed SwiGLU copy costs 2 * 11008 * 4096 * 2 B per layer: keep it only with room to spare
+    packed = free > 12e9 and len(mine) <= 128
+    model.model.packed_swiglu_max_tokens = 128 if packed else 0
+    dec = BatchedGreedyDecoder(model, cache, len(mine), use_cuda_graph=True, prefill_chunk=1)
+
+    barrier(world)
+    clocks = ClockSampler(local)
+    clocks.start()
+    p0 = torch.cuda.Event(enable_timing=True)
+    p1 = torch.cuda.Event(enable_timing=True)
+    p0.record()
+    dec.prefill([prompts[i] for i in mine])
+    p1.record()
+    barrier(world)
+    prefill_ms = max_over_ranks(p0.elapsed_time(p1), world)
+    dec.capture()  # one untimed warm-up step inside, state restored
+    barrier(world)
+    d0 = torch.cuda.Event(enable_timing=True)
+    d1 = torch.cuda.Event(enable_timing=True)
+    d0.record()
+    for _ in range(LONG_NEW):
+        dec.graph.replay()
+    d1.record()
+    barrier(world)
+    decode_ms = max_over_ranks(d0.elapsed_time(d1), world)
+    clk = clocks.stop()
+    status = _lib.device_status()
+    dec.release()
+
+    sum_p = sum(lens)
+    prefill_flops = 2 * 6.476e9 * sum_p + 2 * 32 * 128 * 32 * sum(n * n for n in lens)
+    decode_tokens = LONG_SEQS * LONG_NEW
+    # bytes per decode step, summed over ranks: each rank streams the weights
+    # once plus its sequences' K/V (mean context P + 128 over the 256 steps)
+    kv_bytes = sum(n + LONG_NEW // 2 for n in lens) * KV_BYTES_PER_TOKEN_7B
+    step_bytes = world * WEIGHT_BYTES_7B + kv_bytes
+    pk = _peaks()
+    hbm = pk.get("hbm_gbs_sustained", pk.get("hbm_gbs", 6650.0))
+    tc = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops", 1590.0))
+    step_ms = decode_ms / LONG_NEW
+    achieved = step_bytes / world / (step_ms / 1e3) / 1e9
+    line = {
+        "metric": "long-context mixed run: prefill tok/s and decode tok/s (7B shape)",
+        "suite": "longctx", "value": round(decode_tokens / (decode_ms / 1e3), 1), "unit": "tok/s",
+        "n_gpus": world, "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
+        "data": "synthetic (random-init weights, uniform random prompt ids)",
+        "config": {"workload": "64 prompts of 1024..8192 tokens (uniform, seed 4), prefill then "
+                               "256 greedy decode steps, ragged KV cache",
+                   "sum_prompt_tokens": sum_p, "prompt_len_min": min(lens),
+                   "prompt_len_max": max(lens), "partition": "LPT on prompt+256",
+                   "rank_loads": loads, "kv_cache_gb_rank0": round(cache.memory_footprint_bytes() / 1e9, 2),
+                   "packed_swiglu": packed},
+        "prefill": {"tokens": sum_p, "ms": round(prefill_ms, 1),
+                    "tok_s": round(sum_p / (prefill_ms / 1e3), 1),
+                    "tflops": round(prefill_flops / (prefill_ms / 1e3) / 1e12 / world, 1),
+                    "frac_tc_per_gpu": round(prefill_flops / (prefill_ms / 1e3) / 1e12 / world / tc, 4),
+                    "flop_model": "2*6.476e9*sum(P) + 2*H*D*L*sum(P^2)"},
+        "decode": {"steps": LONG_NEW, "ms": round(decode_ms, 1), "ms_per_step": round(step_ms, 3),
+                   "tok_s": round(decode_tokens / (decode_ms / 1e3), 1),
+                   "bytes_per_step_all_ranks": int(step_bytes),
+                   "achieved_gbs_per_gpu": round(achieved, 1), "peak_gbs": hbm,
+                   "frac_hbm": round(achieved / hbm, 4)},
+        "clocks": clk, "device_status": status,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.suite == "ops":
         run_ops(args)
+        return
+    if args.suite == "longctx":
+        world, rank, local = dist_setup()
+        try:
+            run_longctx(args, world, rank, local)
+        finally:
+            if world > 1:
+                import torch.distributed as dist
+                dist.destroy_process_group()
         return
     world, rank, local = dist_setup() if torch.cuda.is_available() else (1, 0, 0)
     if args.impl == "reference":

@@ -61,7 +61,7 @@ class _StepContext:
     """Per-forward data shared by all layers (computed once, not per layer)."""
 
     __slots__ = ("positions", "seq_lens", "start_pos", "cos_table", "sin_table", "decode",
-                 "workspace")
+                 "workspace", "packed_max")
 
     def __init__(self):
         self.positions = None
@@ -70,6 +70,7 @@ class _StepContext:
         self.cos_table = None
         self.sin_table = None
         self.decode = False
+        self.packed_max = 0
         self.workspace = None
 
 
@@ -176,11 +177,11 @@ class LlamaDecodeLayer(nn.Module):
             self._packed_key = key
         return self._packed_gate_up
 
-    def _mlp_inter(self, h: torch.Tensor, decode: bool) -> torch.Tensor:
+    def _mlp_inter(self, h: torch.Tensor, packed_max: int) -> torch.Tensor:
         norm = self.post_attention_layernorm
         tokens = h.numel() // h.shape[-1]
         w = self.gate_proj.weight
-        if (decode and tokens <= PACKED_SWIGLU_MAX_TOKENS and h.dtype in (torch.bfloat16, torch.float16)
+        if (tokens <= packed_max and h.dtype in (torch.bfloat16, torch.float16)
                 and w.dtype == h.dtype and h.shape[-1] % 64 == 0):
             # decode-sized: norm, then the weight-streaming GEMM on packed
             # weights with the SiLU*up epilogue (faster than the activation-
@@ -206,7 +207,7 @@ class LlamaDecodeLayer(nn.Module):
         attn = self.self_attn(self.input_layernorm(x), positions=positions, cos=cos, sin=sin,
                               kv_cache=kv_cache, layer_idx=self.layer_idx, mask=mask, ctx=ctx)
         h = self.self_attn.project_out(attn, x)
-        mlp_inter = self._mlp_inter(h, ctx is not None and ctx.decode)
+        mlp_inter = self._mlp_inter(h, ctx.packed_max if ctx is not None and ctx.decode else 0)
         shp = h.shape
         return torch.addmm(h.reshape(-1, shp[-1]), mlp_inter.reshape(-1, mlp_inter.shape[-1]),
                            self.down_proj.weight.t()).view(shp)
@@ -222,6 +223,9 @@ class LlamaModel(nn.Module):
         cos, sin = precompute_freqs_cis(config.head_dim, config.max_seq_len, theta=config.rope_theta)
         self.register_buffer("cos_cached", cos, persistent=False)
         self.register_buffer("sin_cached", sin, persistent=False)
+        # decode steps with at most this many tokens use the packed SwiGLU
+        # weights (0 disables the packed copy, e.g. when HBM is tight)
+        self.packed_swiglu_max_tokens = PACKED_SWIGLU_MAX_TOKENS
 
     def reset_rope_tables(self) -> None:
         """Recompute cos/sin (e.g. after materialising a meta-device model)."""
@@ -244,6 +248,7 @@ class LlamaModel(nn.Module):
         B, S = input_ids.shape
         ctx = _StepContext()
         ctx.positions = positions
+        ctx.packed_max = self.packed_swiglu_max_tokens
         cos = sin = None
         if kv_cache is not None:
             ctx.cos_table, ctx.sin_table = self.cos_cached, self.sin_cached
