@@ -116,6 +116,27 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
   }
 }
 
+// Bounded wait that polls with test_wait (never suspends the thread): for a
+// single issuing thread whose wake-up latency is on the critical path.
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, unsigned int* status) {
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((it & 1023u) == 1023u && global_timer_ns() - t0 > LPC_WAIT_LIMIT_NS) {
+      atomicOr(status, LPC_DEV_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // 1-D bulk copy global -> shared, completion signalled as tx bytes on `bar`.
 // Both addresses 16-byte aligned, size a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,

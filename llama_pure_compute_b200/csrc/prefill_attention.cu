@@ -299,13 +299,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int i = 0; i < BKV; ++i)
           if (i > lim_rel) sv[i] = 0xff800000u;  // -inf
       }
-      float m0 = -INFINITY, m1 = -INFINITY;
+      // row max: four independent chains of 3-input max
+      float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < BKV; i += 4) {
+      for (int i = 0; i < BKV; i += 8) {
         m0 = max3(m0, __uint_as_float(sv[i]), __uint_as_float(sv[i + 1]));
         m1 = max3(m1, __uint_as_float(sv[i + 2]), __uint_as_float(sv[i + 3]));
+        m2 = max3(m2, __uint_as_float(sv[i + 4]), __uint_as_float(sv[i + 5]));
+        m3 = max3(m3, __uint_as_float(sv[i + 6]), __uint_as_float(sv[i + 7]));
       }
-      const float mt = fmaxf(m0, m1) * p.scale_log2;  // scale > 0
+      const float mt = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * p.scale_log2;  // scale > 0
       // PV_t(j-1) must be done: its P shares these TMEM columns and O must be stable
       if (j >= 1 && !lpc::mbar_wait(o_done(t), (uint32_t)(j - 1) & 1u, st)) { ok = false; break; }
       lpc::tc_fence_after();
@@ -319,24 +322,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         rescale = true;
       }
       const float m_use = m_used == -INFINITY ? 0.f : m_used;
-      // e = exp2(s * scale - m) two at a time: packed fma, packed row-sum add
+      // e = exp2(s * scale - m), two at a time (packed fma, packed row-sum
+      // adds on two chains), all 128 before the TMEM stores.
       const uint64_t sc2 = pack_f2(p.scale_log2, p.scale_log2);
       const uint64_t nm2 = pack_f2(-m_use, -m_use);
-      uint64_t rs2 = 0;
+      uint64_t rsa = 0, rsb = 0;
+      uint32_t pk[BKV / 2];
 #pragma unroll
-      for (int c = 0; c < BKV; c += 32) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const uint64_t x2 = fma_f2(pack_u2(sv[c + i], sv[c + i + 1]), sc2, nm2);
-          const float e0 = fast_exp2(lo_f(x2));
-          const float e1 = fast_exp2(hi_f(x2));
-          const uint64_t e2 = pack_f2(e0, e1);
-          rs2 = add_f2(rs2, e2);
-          pk[i >> 1] = pack2<T>(e0, e1);
-        }
-        lpc::tmem_st16(tS + (uint32_t)(c >> 1), pk);
+      for (int i = 0; i < BKV; i += 2) {
+        const uint64_t x = fma_f2(pack_u2(sv[i], sv[i + 1]), sc2, nm2);
+        const uint64_t e = pack_f2(fast_exp2(lo_f(x)), fast_exp2(hi_f(x)));
+        if ((i >> 1) & 1) rsb = add_f2(rsb, e);
+        else rsa = add_f2(rsa, e);
+        pk[i >> 1] = pack2<T>(lo_f(e), hi_f(e));
       }
+#pragma unroll
+      for (int c = 0; c < BKV / 2; c += 16)
+        lpc::tmem_st16(tS + (uint32_t)c, *reinterpret_cast<uint32_t(*)[16]>(&pk[c]));
+      const uint64_t rs2 = add_f2(rsa, rsb);
       const float rs = lo_f(rs2) + hi_f(rs2);
       l = l * alpha + rs;
       if (__any_sync(0xffffffffu, rescale)) {
