@@ -6,7 +6,11 @@
 // tests/test_attention_correctness.py:10-76 and the causal prefill kernel of
 // src/llama_pure_compute/triton_kernels/flash_attention.py:88-432.
 //
-// One CTA per (256 queries = two 128-row tiles, head, batch); 10 warps:
+// Persistent: one CTA per SM loops over work items (256 queries = two
+// 128-row tiles, head, batch), longest causal blocks first, dealt to the CTAs
+// in snake order; the next item's Q/K/V loads and first QK^T MMAs overlap the
+// current item's last tiles and epilogue (one CTA holds all 512 TMEM columns,
+// so consecutive CTAs on an SM could not overlap).  10 warps:
 //   warp 8     TMA producer: Q0/Q1 once (64-column boxes), then K and V
 //              128-key tiles into 2-stage rings (4-D tensor maps: rows past
 //              kv_len / q_len read as zeros).  K/V tiles serve both Q tiles.
@@ -26,7 +30,9 @@
 // TMEM (512 columns): S0/P0 [0,128), S1/P1 [128,256), O0 [256,384), O1 [384,512).
 // MMAs issued by one thread execute in order, so S_t of key tile j+1 never
 // overwrites P_t of tile j before PV_t(j) has read it.
-// Causal key tiles past the diagonal are skipped; q blocks run longest first.
+// Causal key tiles past the diagonal are skipped.  Barrier phases are counted
+// across items: q_empty (all S MMAs of an item done with Q) releases the Q
+// buffer for the next item, o_free (epilogue has read O_t) gates its first PV_t.
 #include <atomic>
 
 #include "lpc_common.cuh"
@@ -116,10 +122,43 @@ __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
 
 struct Params {
   int64_t q_len, kv_len, offset;  // offset = kv_len - q_len
-  int heads, kv_heads, group, num_q_blocks;
+  int heads, kv_heads, group, num_q_blocks, batch;
+  int num_items;                  // num_q_blocks * heads * batch
   float scale_log2;
   int causal;
 };
+
+// Work item `i` in longest-first order: query block (descending), head, batch.
+struct Item {
+  int qb, h, b;
+  int64_t q0;
+  int n0, n1;  // key tiles needed by query tile 0 / 1 (tile 1 sees the most keys)
+};
+
+__device__ __forceinline__ Item decode_item(const Params& p, int i) {
+  Item it;
+  const int hb = p.heads * p.batch;
+  it.qb = p.num_q_blocks - 1 - i / hb;
+  const int r = i - (i / hb) * hb;
+  it.h = r % p.heads;
+  it.b = r / p.heads;
+  it.q0 = (int64_t)it.qb * (NQT * BQ);
+  const int64_t all = (p.kv_len + BKV - 1) / BKV;
+  int64_t n0 = all, n1 = all;
+  if (p.causal) {
+    n0 = min(all, (p.offset + it.q0 + BQ - 1) / BKV + 1);
+    n1 = min(all, (p.offset + it.q0 + 2 * BQ - 1) / BKV + 1);
+  }
+  it.n0 = (int)n0;
+  it.n1 = (int)n1;
+  return it;
+}
+
+// The r-th work item of CTA c in a grid of G CTAs: rows of G items taken in
+// snake order (c, 2G-1-c, 2G+c, ...), which balances longest-first items.
+__device__ __forceinline__ int item_of(int c, int G, int r) {
+  return r * G + ((r & 1) ? (G - 1 - c) : c);
+}
 
 template <typename T>
 __global__ void __launch_bounds__(NTHREADS, 1)
@@ -134,6 +173,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t sV = sK + KV_STAGES * TILE_BYTES;          // KV_STAGES
   const uint32_t bars = sV + KV_STAGES * TILE_BYTES;
   const uint32_t q_full = bars;
+  const uint32_t q_empty = bars + 8u * 19;                   // all S MMAs of an item done with Q
   auto k_full = [&](int s) { return bars + 8u * (1 + s); };
   auto k_empty = [&](int s) { return bars + 8u * (3 + s); };
   auto v_full = [&](int s) { return bars + 8u * (5 + s); };
@@ -141,28 +181,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   auto s_full = [&](int t) { return bars + 8u * (9 + t); };
   auto p_full = [&](int t) { return bars + 8u * (11 + t); };
   auto o_done = [&](int t) { return bars + 8u * (13 + t); };
-  const uint32_t tmem_slot = bars + 8u * 15;
+  auto o_free = [&](int t) { return bars + 8u * (15 + t); };  // epilogue has read O_t
+  const uint32_t tmem_slot = bars + 8u * 20;
   volatile uint32_t* tmem_slot_ptr =
       reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qb = p.num_q_blocks - 1 - (int)blockIdx.x;  // longest causal rows first
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
-  const int kvh = h / p.group;
-  const int64_t q0 = (int64_t)qb * (NQT * BQ);
-  const int64_t kv_tiles_all = (p.kv_len + BKV - 1) / BKV;
-  // key tiles each query tile needs (the later tile sees the most keys)
-  auto tiles_for = [&](int t) -> int {
-    int64_t n = kv_tiles_all;
-    if (p.causal) n = min(n, (p.offset + q0 + (int64_t)(t + 1) * BQ - 1) / BKV + 1);
-    return (int)n;
-  };
-  const int n_q0 = tiles_for(0);
-  const int n_all = tiles_for(1);
+  const int G = (int)gridDim.x;
+  const int c = (int)blockIdx.x;
 
   if (threadIdx.x == 0) {
     lpc::mbar_init(q_full, 1);
+    lpc::mbar_init(q_empty, 1);
     for (int s = 0; s < KV_STAGES; ++s) {
       lpc::mbar_init(k_full(s), 1);
       lpc::mbar_init(k_empty(s), 1);
@@ -173,6 +203,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       lpc::mbar_init(s_full(t), 1);
       lpc::mbar_init(p_full(t), 4);
       lpc::mbar_init(o_done(t), 1);
+      lpc::mbar_init(o_free(t), 4);
     }
     lpc::fence_mbar_init();
   }
@@ -193,37 +224,49 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   if (warp == 8) {
     // ---------------- TMA producer ----------------
-    if (lane == 0 && n_all > 0) {
-      lpc::mbar_arrive_expect_tx(q_full, NQT * TILE_BYTES);
-      for (int t = 0; t < NQT; ++t) {
-        tma_load_4d(sQ + t * TILE_BYTES, &tmQ, 0, (int)(q0 + t * BQ), h, b, q_full);
-        tma_load_4d(sQ + t * TILE_BYTES + HALF_BYTES, &tmQ, BOX, (int)(q0 + t * BQ), h, b, q_full);
-      }
-      for (int j = 0; j < n_all; ++j) {
-        const int s = j % KV_STAGES;
-        const uint32_t par = ((uint32_t)(j / KV_STAGES) & 1u) ^ 1u;
-        const int k0 = j * BKV;
-        if (!lpc::mbar_wait(k_empty(s), par, st)) break;
-        lpc::mbar_arrive_expect_tx(k_full(s), TILE_BYTES);
-        tma_load_4d(sK + s * TILE_BYTES, &tmK, 0, k0, kvh, b, k_full(s));
-        tma_load_4d(sK + s * TILE_BYTES + HALF_BYTES, &tmK, BOX, k0, kvh, b, k_full(s));
-        if (!lpc::mbar_wait(v_empty(s), par, st)) break;
-        lpc::mbar_arrive_expect_tx(v_full(s), TILE_BYTES);
-        tma_load_4d(sV + s * TILE_BYTES, &tmV, 0, k0, kvh, b, v_full(s));
-        tma_load_4d(sV + s * TILE_BYTES + HALF_BYTES, &tmV, BOX, k0, kvh, b, v_full(s));
+    // Q of the next item as soon as the last S MMA of the previous one is
+    // done; K/V tiles through 2-stage rings counted across items.
+    if (lane == 0) {
+      bool ok = true;
+      uint32_t kvc = 0;
+      for (int r = 0, i = item_of(c, G, 0); i < p.num_items && ok; i = item_of(c, G, ++r)) {
+        const Item it = decode_item(p, i);
+        const int kvh = it.h / p.group;
+        if (!(ok = lpc::mbar_wait(q_empty, ((uint32_t)r & 1u) ^ 1u, st))) break;
+        lpc::mbar_arrive_expect_tx(q_full, NQT * TILE_BYTES);
+        for (int t = 0; t < NQT; ++t) {
+          tma_load_4d(sQ + t * TILE_BYTES, &tmQ, 0, (int)(it.q0 + t * BQ), it.h, it.b, q_full);
+          tma_load_4d(sQ + t * TILE_BYTES + HALF_BYTES, &tmQ, BOX, (int)(it.q0 + t * BQ), it.h,
+                      it.b, q_full);
+        }
+        for (int j = 0; j < it.n1; ++j, ++kvc) {
+          const int s = kvc % KV_STAGES;
+          const uint32_t par = ((kvc / KV_STAGES) & 1u) ^ 1u;
+          const int k0 = j * BKV;
+          if (!(ok = lpc::mbar_wait(k_empty(s), par, st))) break;
+          lpc::mbar_arrive_expect_tx(k_full(s), TILE_BYTES);
+          tma_load_4d(sK + s * TILE_BYTES, &tmK, 0, k0, kvh, it.b, k_full(s));
+          tma_load_4d(sK + s * TILE_BYTES + HALF_BYTES, &tmK, BOX, k0, kvh, it.b, k_full(s));
+          if (!(ok = lpc::mbar_wait(v_empty(s), par, st))) break;
+          lpc::mbar_arrive_expect_tx(v_full(s), TILE_BYTES);
+          tma_load_4d(sV + s * TILE_BYTES, &tmV, 0, k0, kvh, it.b, v_full(s));
+          tma_load_4d(sV + s * TILE_BYTES + HALF_BYTES, &tmV, BOX, k0, kvh, it.b, v_full(s));
+        }
       }
     }
   } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
-    // Issue order per key tile j:  PV0(j), S0(j+1), PV1(j), S1(j+1).  While
-    // warpgroup 0 exponentiates S0(j+1) the tensor core runs PV1(j) and
-    // S1(j+1), and the other way round: the two softmax warpgroups alternate
-    // with the tensor core instead of waiting for it together.
-    if (lane == 0 && n_all > 0) {
-      bool ok = lpc::mbar_wait(q_full, 0, st);
-      auto issue_s = [&](int t, int j) -> bool {
-        const int s = j % KV_STAGES;
-        if (!lpc::mbar_wait(k_full(s), (uint32_t)(j / KV_STAGES) & 1u, st)) return false;
+    // Per item, issue order per key tile j:  PV0(j), S0(j+1), PV1(j), S1(j+1).
+    // While warpgroup 0 exponentiates S0(j+1) the tensor core runs PV1(j) and
+    // S1(j+1), and the other way round.  Across items: S_t(0) of the next item
+    // is issued right after the last PV_t of the current one; PV_t(0) waits
+    // until the epilogue has read O_t (o_free).
+    if (lane == 0) {
+      bool ok = true;
+      uint32_t kvc = 0, c0 = 0, c1 = 0;  // key tiles / S_0 tiles / S_1 tiles so far
+      auto issue_s = [&](int t, uint32_t kv) -> bool {
+        const int s = kv % KV_STAGES;
+        if (!lpc::mbar_wait(k_full(s), (kv / KV_STAGES) & 1u, st)) return false;
         lpc::tc_fence_after();
         const uint32_t kb = sK + s * TILE_BYTES;
         const uint32_t qt = sQ + t * TILE_BYTES;
@@ -238,10 +281,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         lpc::umma_commit(s_full(t));
         return true;
       };
-      auto issue_pv = [&](int t, int j) -> bool {
-        const int s = j % KV_STAGES;
-        if (!lpc::mbar_wait(p_full(t), (uint32_t)j & 1u, st)) return false;
-        if (!lpc::mbar_wait(v_full(s), (uint32_t)(j / KV_STAGES) & 1u, st)) return false;
+      auto issue_pv = [&](int t, uint32_t kv, uint32_t pc, bool first) -> bool {
+        const int s = kv % KV_STAGES;
+        if (!lpc::mbar_wait(p_full(t), pc & 1u, st)) return false;
+        if (!lpc::mbar_wait(v_full(s), (kv / KV_STAGES) & 1u, st)) return false;
         lpc::tc_fence_after();
         const uint32_t vb = sV + s * TILE_BYTES;
 #pragma unroll
@@ -249,137 +292,169 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           // A: P_t in TMEM (16 keys = 8 columns of packed pairs); B: V rows = keys
           const uint64_t bd = lpc::smem_desc_sw128(vb + kk * 16 * 128, HALF_BYTES, 1024);
           lpc::umma_ts(tmem + 256u + 128u * t, tmem + 128u * t + 8u * kk, bd, idesc_pv,
-                       (j | kk) != 0);
+                       (!first) || kk != 0);
         }
         lpc::umma_commit(o_done(t));
         return true;
       };
-      if (ok && n_q0 > 0) ok = issue_s(0, 0);
-      if (ok) ok = issue_s(1, 0);
-      if (ok) lpc::umma_commit(k_empty(0));
-      for (int j = 0; j < n_all && ok; ++j) {
-        if (j < n_q0 && !(ok = issue_pv(0, j))) break;
-        if (j + 1 < n_q0 && !(ok = issue_s(0, j + 1))) break;
-        if (!(ok = issue_pv(1, j))) break;
-        lpc::umma_commit(v_empty(j % KV_STAGES));
-        if (j + 1 < n_all) {
-          if (!(ok = issue_s(1, j + 1))) break;
-          lpc::umma_commit(k_empty((j + 1) % KV_STAGES));
+      for (int r = 0, i = item_of(c, G, 0); i < p.num_items && ok; i = item_of(c, G, ++r)) {
+        const Item it = decode_item(p, i);
+        if (!(ok = lpc::mbar_wait(q_full, (uint32_t)r & 1u, st))) break;
+        lpc::tc_fence_after();
+        if (!(ok = issue_s(0, kvc) && issue_s(1, kvc))) break;
+        lpc::umma_commit(k_empty(kvc % KV_STAGES));
+        if (it.n1 == 1) lpc::umma_commit(q_empty);  // the last S MMA of the item has read Q
+        // O_t of the previous item must have been read out before PV_t(0) of this one
+        auto o_ready = [&](int t) -> bool {
+          return r == 0 || lpc::mbar_wait(o_free(t), (uint32_t)(r - 1) & 1u, st);
+        };
+        for (int j = 0; j < it.n1 && ok; ++j) {
+          const uint32_t kv = kvc + (uint32_t)j;
+          if (j < it.n0) {
+            if (j == 0 && !(ok = o_ready(0))) break;
+            if (!(ok = issue_pv(0, kv, c0 + (uint32_t)j, j == 0))) break;
+          }
+          if (j + 1 < it.n0 && !(ok = issue_s(0, kv + 1))) break;
+          if (j == 0 && !(ok = o_ready(1))) break;
+          if (!(ok = issue_pv(1, kv, c1 + (uint32_t)j, j == 0))) break;
+          lpc::umma_commit(v_empty(kv % KV_STAGES));
+          if (j + 1 < it.n1) {
+            if (!(ok = issue_s(1, kv + 1))) break;
+            lpc::umma_commit(k_empty((kv + 1) % KV_STAGES));
+            if (j + 2 == it.n1) lpc::umma_commit(q_empty);  // last S MMA of the item issued
+          }
         }
+        kvc += (uint32_t)it.n1;
+        c0 += (uint32_t)it.n0;
+        c1 += (uint32_t)it.n1;
       }
     }
   } else {
     // ---------------- softmax + epilogue: warpgroup t = warp / 4 ----------------
     const int t = warp >> 2;
-    const int r = (warp & 3) * 32 + lane;          // row within the query tile = TMEM lane
-    const int64_t qrow = q0 + (int64_t)t * BQ + r;  // query index
-    const int64_t qpos = p.offset + qrow;           // absolute position
+    const int rr = (warp & 3) * 32 + lane;         // row within the query tile = TMEM lane
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + 128u * t + lane_off;
     const uint32_t tO = tmem + 256u + 128u * t + lane_off;
-    const int n = t == 0 ? n_q0 : n_all;
-    const int64_t lim = p.causal ? min(qpos, p.kv_len - 1) : p.kv_len - 1;  // last visible key
-    float m_used = -INFINITY, l = 0.f;
-    bool ok = n > 0;
-    for (int j = 0; j < n && ok; ++j) {
-      if (!lpc::mbar_wait(s_full(t), (uint32_t)j & 1u, st)) { ok = false; break; }
-      lpc::tc_fence_after();
-      const int64_t k0 = (int64_t)j * BKV;
-      const bool need_mask =
-          (k0 + BKV > p.kv_len) || (p.causal && k0 + BKV - 1 > p.offset + q0 + (int64_t)t * BQ);
-      uint32_t sv[BKV];
+    bool ok = true;
+    uint32_t cnt = 0;  // S_t tiles so far (phase of s_full / p_full / o_done)
+    // bounded wait with a warp-uniform outcome: a warp never splits on a
+    // timeout, so the __syncwarp calls below always see the whole warp
+    auto wait_warp = [&](uint32_t bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, lpc::mbar_wait(bar, parity, st));
+    };
+    for (int r = 0, i = item_of(c, G, 0); i < p.num_items && ok; i = item_of(c, G, ++r)) {
+      const Item it = decode_item(p, i);
+      const int n = t == 0 ? it.n0 : it.n1;
+      const int64_t qrow = it.q0 + (int64_t)t * BQ + rr;  // query index
+      const int64_t qpos = p.offset + qrow;               // absolute position
+      const int64_t lim = p.causal ? min(qpos, p.kv_len - 1) : p.kv_len - 1;  // last visible key
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < n && ok; ++j) {
+        const uint32_t ph = cnt + (uint32_t)j;
+        if (!wait_warp(s_full(t), ph & 1u)) { ok = false; break; }
+        lpc::tc_fence_after();
+        const int64_t k0 = (int64_t)j * BKV;
+        const bool need_mask = (k0 + BKV > p.kv_len) ||
+                               (p.causal && k0 + BKV - 1 > p.offset + it.q0 + (int64_t)t * BQ);
+        uint32_t sv[BKV];
 #pragma unroll
-      for (int c = 0; c < BKV; c += 32)
-        lpc::tmem_ld32(tS + c, *reinterpret_cast<uint32_t(*)[32]>(&sv[c]));
-      lpc::tmem_wait_ld();
-      if (need_mask) {
-        // keys k0 + i with i > lim - k0 are invisible to this row
-        const int lim_rel = (int)max((int64_t)-1, min(lim - k0, (int64_t)(BKV - 1)));
-#pragma unroll
-        for (int i = 0; i < BKV; ++i)
-          if (i > lim_rel) sv[i] = 0xff800000u;  // -inf
-      }
-      // row max: four independent chains of 3-input max
-      float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < BKV; i += 8) {
-        m0 = max3(m0, __uint_as_float(sv[i]), __uint_as_float(sv[i + 1]));
-        m1 = max3(m1, __uint_as_float(sv[i + 2]), __uint_as_float(sv[i + 3]));
-        m2 = max3(m2, __uint_as_float(sv[i + 4]), __uint_as_float(sv[i + 5]));
-        m3 = max3(m3, __uint_as_float(sv[i + 6]), __uint_as_float(sv[i + 7]));
-      }
-      const float mt = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * p.scale_log2;  // scale > 0
-      // PV_t(j-1) must be done: its P shares these TMEM columns and O must be stable
-      if (j >= 1 && !lpc::mbar_wait(o_done(t), (uint32_t)(j - 1) & 1u, st)) { ok = false; break; }
-      lpc::tc_fence_after();
-      float alpha = 1.f;
-      bool rescale = false;
-      if (j == 0) {
-        m_used = mt;
-      } else if (mt > m_used + RESCALE_THRESHOLD) {
-        alpha = fast_exp2(m_used - mt);
-        m_used = mt;
-        rescale = true;
-      }
-      const float m_use = m_used == -INFINITY ? 0.f : m_used;
-      // e = exp2(s * scale - m), two at a time (packed fma, packed row-sum
-      // adds on two chains), all 128 before the TMEM stores.
-      const uint64_t sc2 = pack_f2(p.scale_log2, p.scale_log2);
-      const uint64_t nm2 = pack_f2(-m_use, -m_use);
-      uint64_t rsa = 0, rsb = 0;
-      uint32_t pk[BKV / 2];
-#pragma unroll
-      for (int i = 0; i < BKV; i += 2) {
-        const uint64_t x = fma_f2(pack_u2(sv[i], sv[i + 1]), sc2, nm2);
-        const uint64_t e = pack_f2(fast_exp2(lo_f(x)), fast_exp2(hi_f(x)));
-        if ((i >> 1) & 1) rsb = add_f2(rsb, e);
-        else rsa = add_f2(rsa, e);
-        pk[i >> 1] = pack2<T>(lo_f(e), hi_f(e));
-      }
-#pragma unroll
-      for (int c = 0; c < BKV / 2; c += 16)
-        lpc::tmem_st16(tS + (uint32_t)c, *reinterpret_cast<uint32_t(*)[16]>(&pk[c]));
-      const uint64_t rs2 = add_f2(rsa, rsb);
-      const float rs = lo_f(rs2) + hi_f(rs2);
-      l = l * alpha + rs;
-      if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll 1
-        for (int c = 0; c < HD; c += 16) {
-          uint32_t v[16];
-          lpc::tmem_ld16(tO + c, v);
-          lpc::tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-          lpc::tmem_st16(tO + c, v);
-        }
-      }
-      lpc::tmem_wait_st();
-      lpc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) lpc::mbar_arrive(p_full(t));
-    }
-    // epilogue: O / l
-    if (ok && lpc::mbar_wait(o_done(t), (uint32_t)(n - 1) & 1u, st)) {
-      lpc::tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      const bool valid = qrow < p.q_len;
-      T* orow = out + (((int64_t)b * p.heads + h) * p.q_len + qrow) * HD;
-#pragma unroll 1
-      for (int c = 0; c < HD; c += 32) {
-        uint32_t v[32];
-        lpc::tmem_ld32(tO + c, v);
+        for (int cc = 0; cc < BKV; cc += 32)
+          lpc::tmem_ld32(tS + cc, *reinterpret_cast<uint32_t(*)[32]>(&sv[cc]));
         lpc::tmem_wait_ld();
-        if (valid) {
-          uint32_t pk[16];
+        if (need_mask) {
+          // keys k0 + i with i > lim - k0 are invisible to this row
+          const int lim_rel = (int)max((int64_t)-1, min(lim - k0, (int64_t)(BKV - 1)));
 #pragma unroll
-          for (int i = 0; i < 32; i += 2)
-            pk[i >> 1] = pack2<T>(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv);
-          uint4* dst = reinterpret_cast<uint4*>(orow + c);
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4)
-            dst[q4] = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+          for (int q = 0; q < BKV; ++q)
+            if (q > lim_rel) sv[q] = 0xff800000u;  // -inf
         }
+        // row max: four independent chains of 3-input max
+        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+#pragma unroll
+        for (int q = 0; q < BKV; q += 8) {
+          m0 = max3(m0, __uint_as_float(sv[q]), __uint_as_float(sv[q + 1]));
+          m1 = max3(m1, __uint_as_float(sv[q + 2]), __uint_as_float(sv[q + 3]));
+          m2 = max3(m2, __uint_as_float(sv[q + 4]), __uint_as_float(sv[q + 5]));
+          m3 = max3(m3, __uint_as_float(sv[q + 6]), __uint_as_float(sv[q + 7]));
+        }
+        const float mt = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * p.scale_log2;  // scale > 0
+        // PV_t(j-1) must be done: its P shares these TMEM columns and O must be stable
+        if (j >= 1 && !wait_warp(o_done(t), (ph - 1u) & 1u)) { ok = false; break; }
+        lpc::tc_fence_after();
+        float alpha = 1.f;
+        bool rescale = false;
+        if (j == 0) {
+          m_used = mt;
+        } else if (mt > m_used + RESCALE_THRESHOLD) {
+          alpha = fast_exp2(m_used - mt);
+          m_used = mt;
+          rescale = true;
+        }
+        const float m_use = m_used == -INFINITY ? 0.f : m_used;
+        // e = exp2(s * scale - m), two at a time (packed fma, packed row-sum
+        // adds on two chains), all 128 before the TMEM stores.
+        const uint64_t sc2 = pack_f2(p.scale_log2, p.scale_log2);
+        const uint64_t nm2 = pack_f2(-m_use, -m_use);
+        uint64_t rsa = 0, rsb = 0;
+        uint32_t pk[BKV / 2];
+#pragma unroll
+        for (int q = 0; q < BKV; q += 2) {
+          const uint64_t x = fma_f2(pack_u2(sv[q], sv[q + 1]), sc2, nm2);
+          const uint64_t e = pack_f2(fast_exp2(lo_f(x)), fast_exp2(hi_f(x)));
+          if ((q >> 1) & 1) rsb = add_f2(rsb, e);
+          else rsa = add_f2(rsa, e);
+          pk[q >> 1] = pack2<T>(lo_f(e), hi_f(e));
+        }
+#pragma unroll
+        for (int cc = 0; cc < BKV / 2; cc += 16)
+          lpc::tmem_st16(tS + (uint32_t)cc, *reinterpret_cast<uint32_t(*)[16]>(&pk[cc]));
+        const uint64_t rs2 = add_f2(rsa, rsb);
+        const float rs = lo_f(rs2) + hi_f(rs2);
+        l = l * alpha + rs;
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+          for (int cc = 0; cc < HD; cc += 16) {
+            uint32_t v[16];
+            lpc::tmem_ld16(tO + cc, v);
+            lpc::tmem_wait_ld();
+#pragma unroll
+            for (int q = 0; q < 16; ++q) v[q] = __float_as_uint(__uint_as_float(v[q]) * alpha);
+            lpc::tmem_st16(tO + cc, v);
+          }
+        }
+        lpc::tmem_wait_st();
+        lpc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) lpc::mbar_arrive(p_full(t));
       }
+      // epilogue: O / l, then O_t is free for the next item's PV
+      if (ok && (ok = wait_warp(o_done(t), (cnt + (uint32_t)n - 1u) & 1u))) {
+        lpc::tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const bool valid = qrow < p.q_len;
+        T* orow = out + (((int64_t)it.b * p.heads + it.h) * p.q_len + qrow) * HD;
+#pragma unroll 1
+        for (int cc = 0; cc < HD; cc += 32) {
+          uint32_t v[32];
+          lpc::tmem_ld32(tO + cc, v);
+          lpc::tmem_wait_ld();
+          if (valid) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int q = 0; q < 32; q += 2)
+              pk[q >> 1] = pack2<T>(__uint_as_float(v[q]) * inv, __uint_as_float(v[q + 1]) * inv);
+            uint4* dst = reinterpret_cast<uint4*>(orow + cc);
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4)
+              dst[q4] = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+          }
+        }
+        lpc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) lpc::mbar_arrive(o_free(t));
+      }
+      cnt += (uint32_t)n;
     }
   }
   lpc::tc_fence_before();
@@ -456,13 +531,21 @@ extern "C" int lpc_flash_attention(const void* q, const void* k, const void* v, 
   p.kv_heads = kv_heads;
   p.group = heads / kv_heads;
   p.num_q_blocks = (int)((q_len + NQT * BQ - 1) / (NQT * BQ));
+  p.batch = (int)batch;
+  const int64_t items = (int64_t)p.num_q_blocks * heads * batch;
+  if (items > 0x7fffffffLL) {
+    set_error("flash_attention: too many query blocks");
+    return LPC_ERR_UNSUPPORTED;
+  }
+  p.num_items = (int)items;
   p.scale_log2 = sm_scale * LOG2E;
   p.causal = causal ? 1 : 0;
   const uint32_t fmt = dtype == LPC_DTYPE_BF16 ? 1u : 0u;
   const uint32_t id_qk = idesc_f16(fmt, BQ, BKV, 0u, 0u);
   const uint32_t id_pv = idesc_f16(fmt, BQ, HD, 0u, 1u);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  dim3 grid((unsigned)p.num_q_blocks, (unsigned)heads, (unsigned)batch);
+  // persistent: one CTA per SM loops over the work items
+  dim3 grid((unsigned)std::min<int64_t>(items, current_device_sms()));
   int rc;
   if (dtype == LPC_DTYPE_BF16) {
     static std::atomic<uint64_t> mask{0};
