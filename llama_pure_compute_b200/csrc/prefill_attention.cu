@@ -264,19 +264,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (lane == 0) {
       bool ok = true;
       uint32_t kvc = 0, c0 = 0, c1 = 0;  // key tiles / S_0 tiles / S_1 tiles so far
+      // Shared-memory descriptors, built once: a descriptor's start-address
+      // field holds address >> 4, so a byte offset inside a tile is added as
+      // offset >> 4 (16 elements along K: +2; next 64-column half: +HALF/16).
+      const uint64_t dQ = lpc::smem_desc_sw128(sQ, 16, 1024);
+      const uint64_t dK = lpc::smem_desc_sw128(sK, 16, 1024);
+      const uint64_t dV = lpc::smem_desc_sw128(sV, HALF_BYTES, 1024);
       auto issue_s = [&](int t, uint32_t kv) -> bool {
         const int s = kv % KV_STAGES;
         if (!lpc::mbar_wait(k_full(s), (kv / KV_STAGES) & 1u, st)) return false;
         lpc::tc_fence_after();
-        const uint32_t kb = sK + s * TILE_BYTES;
-        const uint32_t qt = sQ + t * TILE_BYTES;
+        const uint64_t aq = dQ + (uint64_t)((t * TILE_BYTES) >> 4);
+        const uint64_t bk = dK + (uint64_t)((s * TILE_BYTES) >> 4);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint64_t ad =
-              lpc::smem_desc_sw128(qt + (kk >> 2) * HALF_BYTES, 16, 1024) + 2u * (kk & 3);
-          const uint64_t bd =
-              lpc::smem_desc_sw128(kb + (kk >> 2) * HALF_BYTES, 16, 1024) + 2u * (kk & 3);
-          lpc::umma_ss(tmem + 128u * t, ad, bd, idesc_qk, kk != 0);
+          const uint32_t off = (uint32_t)(((kk >> 2) * HALF_BYTES) >> 4) + 2u * (kk & 3);
+          lpc::umma_ss(tmem + 128u * t, aq + off, bk + off, idesc_qk, kk != 0);
         }
         lpc::umma_commit(s_full(t));
         return true;
@@ -286,13 +289,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (!lpc::mbar_wait(p_full(t), pc & 1u, st)) return false;
         if (!lpc::mbar_wait(v_full(s), (kv / KV_STAGES) & 1u, st)) return false;
         lpc::tc_fence_after();
-        const uint32_t vb = sV + s * TILE_BYTES;
+        const uint64_t bv = dV + (uint64_t)((s * TILE_BYTES) >> 4);
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk) {
           // A: P_t in TMEM (16 keys = 8 columns of packed pairs); B: V rows = keys
-          const uint64_t bd = lpc::smem_desc_sw128(vb + kk * 16 * 128, HALF_BYTES, 1024);
-          lpc::umma_ts(tmem + 256u + 128u * t, tmem + 128u * t + 8u * kk, bd, idesc_pv,
-                       (!first) || kk != 0);
+          lpc::umma_ts(tmem + 256u + 128u * t, tmem + 128u * t + 8u * kk,
+                       bv + (uint64_t)((kk * 16 * 128) >> 4), idesc_pv, (!first) || kk != 0);
         }
         lpc::umma_commit(o_done(t));
         return true;
