@@ -242,8 +242,14 @@ LPC_API int lpc_decode_attention_noalloc(const void* q, const void* key_cache,
  *           [n_out, k] and up rows from W1 [n_out, k], or from W0 rows
  *           n_out..2*n_out-1 when W1 is NULL (the fused gate_up layout that
  *           rmsswiglu_forward accepts, ops.py:118-131).
+ * layout 2: attention heads, W0 [(H + 2*Hkv) * 128, k] (the q, k and v
+ *           projection weights stacked, head_dim 128); each head's rows are
+ *           interleaved so that the rotate-half partners d and d + 64 meet in
+ *           one warp of the epilogue (lpc_qkv_rope_append).
  * packed: lpc_packed_weight_bytes(n_out, k, layout) bytes, 16-byte aligned.
- * k must be a multiple of 64; bf16 or fp16.
+ * k must be a multiple of 64; bf16 or fp16.  Returns after the packed copy is
+ * complete (the call synchronises `stream`): lpc_wsgemm starts reading the
+ * weights before it waits on the previous kernel of its stream.
  */
 LPC_API int64_t lpc_packed_weight_bytes(int64_t n_out, int k, int layout);
 LPC_API int lpc_pack_weights(const void* w0, const void* w1, void* packed, int64_t n_out, int k,
@@ -262,9 +268,40 @@ LPC_API int lpc_pack_weights(const void* w0, const void* w1, void* packed, int64
  * epilogue 2: out = silu(x Wg^T) * (x Wu^T)    (packed with layout 1; out [tokens, n_out])
  * x: [tokens, k] contiguous; fp32 accumulation, one rounding to the dtype.
  * n_out <= 2^24.  No workspace.
+ * Split k: when there are few weight tiles the launch runs clusters of up to
+ * 8 CTAs per tile, each on a share of k, reduce-scattered through
+ * distributed shared memory (deterministic: fixed rank order).  Launched with
+ * programmatic stream serialisation: the prologue and the first weight chunks
+ * overlap the previous kernel on the stream, and nothing that kernel writes
+ * is read before it completes.
  */
 LPC_API int lpc_wsgemm(const void* x, const void* packed_w, void* out, const void* resid,
                        int64_t tokens, int64_t n_out, int k, int epilogue, int dtype, void* stream);
+
+/*
+ * Fused projection + RoPE + KV append of the attention block for decode-sized
+ * token counts (batch * seq <= 256):
+ *   qkv = x W^T  (W packed with layout 2, rounded to the dtype), then exactly
+ *   lpc_rope_kv_append on it: q rotated into q_out [batch, H, seq, 128], k
+ *   rotated and v copied into the cache row of (b, positions[b, s]).
+ * Replaces: the q/k/v projections, RoPE and the KV update of
+ *           LlamaAttention.forward (model.py:125-168, kv_manager.py:207-317)
+ *           in one kernel: no qkv intermediate, no second launch.
+ * x: [batch * seq, k] (the normed hidden states); positions [batch, seq]
+ * int64 (< 0: the token is skipped); cos/sin [table_rows, 128] in the data
+ * dtype (the model's cos_cached / sin_cached).  Cache layouts as in
+ * lpc_rope_kv_append (seq_base == NULL: dense [max_batch, Hkv, max_seq_len,
+ * 128]) and lpc_rope_kv_append_ragged ([Hkv, total_rows, 128] at
+ * seq_base[b] + pos, pos < seq_cap[b]).  Out-of-range positions or rows set
+ * LPC_DEV_ERR_BOUNDS and skip the token.  head_dim must be 128; bf16 or fp16.
+ */
+LPC_API int lpc_qkv_rope_append(const void* x, const void* packed_w, const int64_t* positions,
+                                const void* cos, const void* sin, int64_t table_rows, void* q_out,
+                                void* key_cache, void* value_cache, const int64_t* seq_base,
+                                const int32_t* seq_cap, int64_t batch, int64_t seq, int num_heads,
+                                int num_kv_heads, int head_dim, int k, int64_t max_batch,
+                                int64_t max_seq_len, int64_t total_rows, int dtype, int table_dtype,
+                                void* stream);
 
 #ifdef __cplusplus
 }

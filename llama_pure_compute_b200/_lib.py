@@ -56,6 +56,8 @@ SIGNATURES = {
     "lpc_packed_weight_bytes": (_I64, [_I64, _I, _I]),
     "lpc_pack_weights": (_I, [_P, _P, _P, _I64, _I, _I, _I, _P]),
     "lpc_wsgemm": (_I, [_P, _P, _P, _P, _I64, _I64, _I, _I, _I, _P]),
+    "lpc_qkv_rope_append": (_I, [_P, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I, _I,
+                                 _I, _I, _I64, _I64, _I64, _I, _I, _P]),
 }
 
 _lib = None
@@ -66,7 +68,7 @@ KERNELS_PER_CALL = {
     "lpc_update_kv_cache": 1, "lpc_rope_forward": 1, "lpc_rope_kv_append": 1,
     "lpc_rmsnorm_forward": 1, "lpc_rmsswiglu_forward": 2, "lpc_flash_attention": 1,
     "lpc_decode_attention": 2, "lpc_decode_attention_noalloc": 2,
-    "lpc_pack_weights": 1, "lpc_wsgemm": 1, "lpc_rope_kv_append_ragged": 1,
+    "lpc_pack_weights": 1, "lpc_wsgemm": 1, "lpc_qkv_rope_append": 1, "lpc_rope_kv_append_ragged": 1,
     "lpc_decode_attention_ragged": 2,
 }
 launch_count = 0

@@ -116,6 +116,32 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
   }
 }
 
+// Bounded wait with cluster-scope acquire: data that other CTAs of the
+// cluster wrote before their release-arrive on `bar` is visible afterwards.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0u;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
+                                                  unsigned int* status) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((it & 255u) == 0u && global_timer_ns() - t0 > LPC_WAIT_LIMIT_NS) {
+      atomicOr(status, LPC_DEV_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // Bounded wait that polls with test_wait (never suspends the thread): for a
 // single issuing thread whose wake-up latency is on the critical path.
 __device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, unsigned int* status) {
@@ -248,6 +274,24 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* tmap,
       : "memory");
 }
 // All threads of all CTAs of the cluster.
+// Programmatic dependent launch.  pdl_wait: returns once the grids this one
+// depends on have completed and their memory is visible (immediately when the
+// launch was not programmatic).  pdl_trigger: lets a dependent grid launched
+// with programmatic stream serialisation start its prologue; a CTA calls it
+// only after its own TMEM allocation, so a waiting dependent never holds
+// tensor memory this grid still needs.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Split cluster barrier: every thread of every CTA arrives once, then waits once.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
                    "memory");

@@ -19,12 +19,13 @@ from __future__ import annotations
 
 import logging
 from dataclasses import dataclass
-from typing import Tuple, Union
+from typing import Optional, Tuple, Union
 
 import torch
 
 from .flash_attention import flash_attention_v2
-from .ops import decode_attention, decode_attention_workspace, rope_kv_append, update_kv_cache
+from .ops import (decode_attention, decode_attention_workspace, qkv_rope_append, rope_kv_append,
+                  update_kv_cache)
 
 logger = logging.getLogger("llama_pure_compute_b200.kv_manager")
 
@@ -240,14 +241,27 @@ class KVCacheManager:
             ctx.start_pos = int(positions[0, 0].item())
             self.seq_lens[:B] = ctx.start_pos + S
 
-    def attend(self, *, layer_idx: int, qkv: torch.Tensor, positions: torch.Tensor, ctx,
-               num_heads: int, scale: float) -> torch.Tensor:
-        """RoPE + append of ``qkv`` [B, S, (H+2Hkv)*D], then causal attention of
-        the new queries over the cached context; returns [B, S, H*D]."""
-        B, S, _ = qkv.shape
+    def attend(self, *, layer_idx: int, positions: torch.Tensor, ctx, num_heads: int,
+               scale: float, qkv: Optional[torch.Tensor] = None,
+               x: Optional[torch.Tensor] = None, packed_qkv=None) -> torch.Tensor:
+        """RoPE + append of ``qkv`` [B, S, (H+2Hkv)*D] -- or, given the normed
+        hidden states ``x`` and the "heads"-packed q/k/v weight, the projection
+        with RoPE and the append fused in one kernel -- then causal attention
+        of the new queries over the cached context; returns [B, S, H*D]."""
+        if packed_qkv is not None:
+            B, S, _ = x.shape
+            self._check_layer(layer_idx)
+            if B > self.max_batch_size:
+                raise ValueError("batch size exceeds cache capacity")
+            q = qkv_rope_append(x, packed_qkv, positions, ctx.cos_table, ctx.sin_table,
+                                self.k_cache[layer_idx], self.v_cache[layer_idx], num_heads,
+                                self.n_kv_heads)
+        else:
+            B, S, _ = qkv.shape
+            q = self.append_qkv(layer_idx=layer_idx, qkv=qkv, positions=positions,
+                                cos_table=ctx.cos_table, sin_table=ctx.sin_table,
+                                num_heads=num_heads)
         D = self.head_dim
-        q = self.append_qkv(layer_idx=layer_idx, qkv=qkv, positions=positions,
-                            cos_table=ctx.cos_table, sin_table=ctx.sin_table, num_heads=num_heads)
         kc, vc = self.k_cache[layer_idx], self.v_cache[layer_idx]
         if ctx.decode:
             out = decode_attention(q.view(B, num_heads, D), kc, vc, ctx.seq_lens, scale,

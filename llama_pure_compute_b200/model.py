@@ -9,6 +9,9 @@ checkpoints and call sites carry over.  What runs underneath:
                        (cuBLAS through torch; the q/k/v parameters are views of it)
   RoPE + KV append  -> lpc_rope_kv_append (model.py:146-168 fused into one kernel;
                        per-row positions, so batches may be ragged)
+                       decode steps of <= 32 tokens (head_dim 128): projection,
+                       RoPE and KV append in one kernel, lpc_qkv_rope_append,
+                       on a packed copy of the q/k/v weight
   attention         -> decode: lpc_decode_attention over device seq_lens
                        (no per-layer .item() sync, model.py:159-161);
                        prefill / no cache: lpc_flash_attention (tcgen05)
@@ -42,6 +45,10 @@ from .rmsnorm import RMSNorm
 # Decode steps with at most this many tokens run the SwiGLU GEMM on packed
 # weights (lpc_wsgemm); the packed copy of gate/up is built on first use.
 PACKED_SWIGLU_MAX_TOKENS = 128
+# Decode steps with at most this many tokens run the q/k/v projection with
+# RoPE and the KV append in its epilogue (lpc_qkv_rope_append) on a packed
+# copy of the q/k/v weight, built on first use.
+FUSED_QKV_MAX_TOKENS = 32
 
 __all__ = ["precompute_freqs_cis", "LlamaAttention", "LlamaDecodeLayer", "LlamaModel",
            "LlamaForCausalLM"]
@@ -61,7 +68,7 @@ class _StepContext:
     """Per-forward data shared by all layers (computed once, not per layer)."""
 
     __slots__ = ("positions", "seq_lens", "start_pos", "cos_table", "sin_table", "decode",
-                 "workspace", "packed_max")
+                 "workspace", "packed_max", "fused_qkv_max")
 
     def __init__(self):
         self.positions = None
@@ -71,6 +78,7 @@ class _StepContext:
         self.sin_table = None
         self.decode = False
         self.packed_max = 0
+        self.fused_qkv_max = 0
         self.workspace = None
 
 
@@ -90,6 +98,8 @@ class LlamaAttention(nn.Module):
         self.o_proj = nn.Linear(self.num_heads * self.head_dim, self.dim, bias=False)
         self._qkv_key = None
         self._qkv = None
+        self._packed_qkv = None
+        self._packed_qkv_key = None
 
     def qkv_weight(self) -> torch.Tensor:
         """[(H+2Hkv)*D, dim] weight; q/k/v parameters are re-pointed into it once."""
@@ -107,6 +117,25 @@ class LlamaAttention(nn.Module):
             ws = (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
             self._qkv_key = tuple((w.data_ptr(), w._version, w.dtype, w.device) for w in ws)
         return self._qkv
+
+    def packed_qkv(self):
+        """The q/k/v weight in the packed "heads" layout (lpc_pack_weights),
+        built on first use and rebuilt when the weight changes."""
+        from .packed_linear import PackedWeight
+        w = self.qkv_weight()
+        # the stacked weight may be an inference tensor (no version counter):
+        # key on the q/k/v parameters it was built from
+        key = (w.data_ptr(), self._qkv_key)
+        if self._packed_qkv is None or key != self._packed_qkv_key:
+            self._packed_qkv = PackedWeight(w, layout="heads")
+            self._packed_qkv_key = key
+        return self._packed_qkv
+
+    def _fused_qkv(self, x: torch.Tensor, ctx: Optional[_StepContext]) -> bool:
+        return (ctx is not None and ctx.decode and 0 < x.numel() // x.shape[-1] <= ctx.fused_qkv_max
+                and self.head_dim == 128 and x.dtype in (torch.bfloat16, torch.float16)
+                and ctx.cos_table is not None and ctx.cos_table.dtype == x.dtype
+                and self.q_proj.weight.dtype == x.dtype and x.shape[-1] % 64 == 0)
 
     def forward(
         self,
@@ -128,6 +157,10 @@ class LlamaAttention(nn.Module):
                 "is applied by passing mask=None")
         B, S, _ = x.shape
         H, Hkv, D = self.num_heads, self.num_kv_heads, self.head_dim
+        if kv_cache is not None and self._fused_qkv(x, ctx):
+            # decode-sized: projection + RoPE + KV append in one kernel
+            return kv_cache.attend(layer_idx=layer_idx, x=x, packed_qkv=self.packed_qkv(),
+                                   positions=positions, ctx=ctx, num_heads=H, scale=self.scale)
         qkv = F.linear(x, self.qkv_weight())
         if kv_cache is not None:
             if ctx is None or ctx.cos_table is None:
@@ -226,6 +259,9 @@ class LlamaModel(nn.Module):
         # decode steps with at most this many tokens use the packed SwiGLU
         # weights (0 disables the packed copy, e.g. when HBM is tight)
         self.packed_swiglu_max_tokens = PACKED_SWIGLU_MAX_TOKENS
+        # decode steps with at most this many tokens use the fused q/k/v
+        # projection + RoPE + KV append on a packed q/k/v copy (0 disables it)
+        self.fused_qkv_max_tokens = FUSED_QKV_MAX_TOKENS
 
     def reset_rope_tables(self) -> None:
         """Recompute cos/sin (e.g. after materialising a meta-device model)."""
@@ -249,6 +285,7 @@ class LlamaModel(nn.Module):
         ctx = _StepContext()
         ctx.positions = positions
         ctx.packed_max = self.packed_swiglu_max_tokens
+        ctx.fused_qkv_max = self.fused_qkv_max_tokens
         cos = sin = None
         if kv_cache is not None:
             ctx.cos_table, ctx.sin_table = self.cos_cached, self.sin_cached

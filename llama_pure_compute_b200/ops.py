@@ -31,6 +31,7 @@ __all__ = [
     "rope_kv_append",
     "decode_attention",
     "rope_kv_append_ragged",
+    "qkv_rope_append",
     "decode_attention_ragged",
 ]
 
@@ -394,6 +395,74 @@ def rope_kv_append_ragged(
         _lib.dtype_code(cos_table.dtype, "rope_kv_append_ragged"), _lib.stream_of(qkv))
     _lib.check(rc, "rope_kv_append_ragged")
     _lib.count_launch("lpc_rope_kv_append_ragged")
+    return q_out
+
+
+def qkv_rope_append(
+    x: torch.Tensor,
+    packed_qkv,
+    positions: torch.Tensor,
+    cos_table: torch.Tensor,
+    sin_table: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    num_heads: int,
+    num_kv_heads: int,
+    seq_base: Optional[torch.Tensor] = None,
+    seq_cap: Optional[torch.Tensor] = None,
+    q_out: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """The attention block's q/k/v projection with RoPE and the KV append in
+    its epilogue (model.py:125-168 + kv_manager.py:260-300 in one kernel).
+
+    ``x`` [B, S, dim] are the normed hidden states, ``packed_qkv`` the stacked
+    q/k/v weight packed with layout "heads" (head_dim 128), B * S <= 256.
+    Equivalent to ``rope_kv_append(x @ W^T, ...)`` (dense cache
+    ``[Bmax, Hkv, Smax, D]``) or ``rope_kv_append_ragged`` (cache
+    ``[Hkv, total_rows, D]`` with ``seq_base`` / ``seq_cap``), with the
+    projection rounded to the dtype before the rotation.  Returns q as
+    [B, H, S, D]."""
+    for t, n in ((x, "x"), (positions, "positions"), (cos_table, "cos"), (sin_table, "sin"),
+                 (key_cache, "key_cache"), (value_cache, "value_cache")):
+        _require_cuda(t, n)
+    if getattr(packed_qkv, "layout", None) != "heads":
+        raise ValueError("LlamaPureComputeError: qkv_rope_append needs a weight packed with "
+                         "layout 'heads'.")
+    if x.dim() != 3:
+        raise ValueError("LlamaPureComputeError: x must be [batch, seq, dim].")
+    B, S, dim = x.shape
+    ragged = seq_base is not None
+    if ragged:
+        Hkv, total_rows, D = key_cache.shape
+        _check_ragged_index(seq_base, seq_cap, B)
+        Bmax = Smax = 0
+    else:
+        Bmax, Hkv, Smax, D = key_cache.shape
+        total_rows = 0
+        if B > Bmax:
+            raise ValueError("LlamaPureComputeError: batch size exceeds cache capacity.")
+    if value_cache.shape != key_cache.shape:
+        raise ValueError("LlamaPureComputeError: key and value caches differ in shape.")
+    if Hkv != num_kv_heads or packed_qkv.n_out != (num_heads + 2 * num_kv_heads) * D:
+        raise ValueError("LlamaPureComputeError: packed weight does not match heads * head_dim.")
+    if dim != packed_qkv.k or x.dtype != packed_qkv.dtype:
+        raise ValueError("LlamaPureComputeError: x must be [..., k] in the weight's dtype.")
+    if cos_table.shape[-1] != D or cos_table.dim() != 2:
+        raise ValueError("LlamaPureComputeError: rope tables must be [max_pos, head_dim].")
+    x = x.contiguous()
+    pos = positions.to(torch.int64).contiguous()
+    if pos.shape != (B, S):
+        raise ValueError("LlamaPureComputeError: positions must be [batch, seq].")
+    if q_out is None:
+        q_out = torch.empty(B, num_heads, S, D, dtype=x.dtype, device=x.device)
+    rc = _lib.load().lpc_qkv_rope_append(
+        x.data_ptr(), packed_qkv.data.data_ptr(), pos.data_ptr(), cos_table.data_ptr(),
+        sin_table.data_ptr(), cos_table.shape[0], q_out.data_ptr(), key_cache.data_ptr(),
+        value_cache.data_ptr(), _lib.ptr(seq_base), _lib.ptr(seq_cap), B, S, num_heads,
+        num_kv_heads, D, dim, Bmax, Smax, total_rows, _lib.dtype_code(x.dtype, "qkv_rope_append"),
+        _lib.dtype_code(cos_table.dtype, "qkv_rope_append"), _lib.stream_of(x))
+    _lib.check(rc, "qkv_rope_append")
+    _lib.count_launch("lpc_qkv_rope_append")
     return q_out
 
 

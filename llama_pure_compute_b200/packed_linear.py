@@ -9,9 +9,12 @@ so the weights are packed once into contiguous tensor-core tiles and each
 projection is one kernel with its epilogue (residual add, SiLU * up) fused.
 
 ``PackedWeight`` owns the packed bytes.  ``packed_linear`` runs one product.
-The kernel runs one CTA per 128-row weight tile over the whole K, so it suits
-wide layers (the SwiGLU gate/up pair, lm_head); narrow ones (o_proj,
-down_proj: 32 tiles for the 7B shape) are left to cuBLAS.
+Layers with few 128-row weight tiles split k over clusters of CTAs (the
+partial tiles are reduce-scattered through distributed shared memory), and
+every launch overlaps its prologue and first weight chunks with the previous
+kernel (programmatic dependent launch).  The packed "heads" layout feeds
+``ops.qkv_rope_append``: the attention block's projection with RoPE and the
+KV append in the epilogue.
 """
 from __future__ import annotations
 
@@ -22,6 +25,7 @@ import torch
 from . import _lib
 
 EPILOGUES = {"store": 0, "residual": 1, "swiglu": 2}
+LAYOUTS = {"linear": 0, "swiglu": 1, "heads": 2}
 MAX_TOKENS = 256
 
 
@@ -32,17 +36,19 @@ class PackedWeight:
     layout "swiglu": ``w0`` holds the gate rows ``[n_out, k]`` and ``w1`` the up
     rows, or ``w1`` is None and ``w0`` is the fused ``[2 n_out, k]`` gate_up
     weight (ops.py:118-131 accepts both forms).
+    layout "heads": ``w0`` is the stacked q/k/v projection weight
+    ``[(H + 2 Hkv) * 128, k]`` (head_dim 128), for ``ops.qkv_rope_append``.
     """
 
     def __init__(self, w0: torch.Tensor, w1: Optional[torch.Tensor] = None,
                  layout: str = "linear"):
-        if layout not in ("linear", "swiglu"):
+        if layout not in LAYOUTS:
             raise ValueError(f"LlamaPureComputeError: unknown packed layout {layout!r}")
         if not w0.is_cuda:
             raise ValueError("LlamaPureComputeError: weights must be on CUDA device.")
         if w0.dim() != 2:
             raise ValueError("LlamaPureComputeError: weight must be 2-D.")
-        lay = 1 if layout == "swiglu" else 0
+        lay = LAYOUTS[layout]
         w0 = w0.detach().contiguous()
         k = w0.shape[1]
         if layout == "swiglu" and w1 is None:
@@ -62,7 +68,8 @@ class PackedWeight:
         nbytes = lib.lpc_packed_weight_bytes(n_out, k, lay)
         if nbytes <= 0:
             raise ValueError(f"LlamaPureComputeError: cannot pack a [{n_out}, {k}] weight "
-                             "(k must be a multiple of 64).")
+                             "(k must be a multiple of 64; layout 'heads' needs n_out a "
+                             "multiple of 128).")
         with torch.cuda.device(w0.device):
             self.data = torch.empty(nbytes, dtype=torch.uint8, device=w0.device)
             rc = lib.lpc_pack_weights(w0.data_ptr(), _lib.ptr(w1), self.data.data_ptr(), n_out, k,
@@ -89,6 +96,8 @@ def packed_linear(x: torch.Tensor, w: PackedWeight, epilogue: str = "store",
         raise ValueError(f"LlamaPureComputeError: unknown epilogue {epilogue!r}")
     if (epilogue == "swiglu") != (w.layout == "swiglu"):
         raise ValueError("LlamaPureComputeError: the swiglu epilogue needs a swiglu-packed weight.")
+    if w.layout == "heads":
+        raise ValueError("LlamaPureComputeError: a 'heads'-packed weight is for qkv_rope_append.")
     if not x.is_cuda:
         raise ValueError("LlamaPureComputeError: x must be on CUDA device.")
     if x.shape[-1] != w.k or x.dtype != w.dtype:

@@ -24,12 +24,13 @@ calls on ``KVCacheManager``; ``LlamaForCausalLM`` takes either cache.
 """
 from __future__ import annotations
 
-from typing import List, Sequence
+from typing import List, Optional, Sequence
 
 import torch
 
 from .flash_attention import flash_attention_v2
-from .ops import decode_attention_ragged, decode_attention_workspace, rope_kv_append_ragged
+from .ops import (decode_attention_ragged, decode_attention_workspace, qkv_rope_append,
+                  rope_kv_append_ragged)
 
 __all__ = ["RaggedKVCache"]
 
@@ -114,13 +115,21 @@ class RaggedKVCache:
             self.active_lens.fill_(end)
         self.seq_lens.index_copy_(0, self._idx, self.active_lens)
 
-    def attend(self, *, layer_idx: int, qkv: torch.Tensor, positions: torch.Tensor, ctx,
-               num_heads: int, scale: float) -> torch.Tensor:
-        B, S, _ = qkv.shape
+    def attend(self, *, layer_idx: int, positions: torch.Tensor, ctx, num_heads: int,
+               scale: float, qkv: Optional[torch.Tensor] = None,
+               x: Optional[torch.Tensor] = None, packed_qkv=None) -> torch.Tensor:
         D = self.head_dim
         kc, vc = self.k_cache[layer_idx], self.v_cache[layer_idx]
-        q = rope_kv_append_ragged(qkv, positions, ctx.cos_table, ctx.sin_table, kc, vc,
-                                  self.active_base, self.active_cap, num_heads, self.n_kv_heads)
+        if packed_qkv is not None:
+            B, S, _ = x.shape
+            q = qkv_rope_append(x, packed_qkv, positions, ctx.cos_table, ctx.sin_table, kc, vc,
+                                num_heads, self.n_kv_heads, seq_base=self.active_base,
+                                seq_cap=self.active_cap)
+        else:
+            B, S, _ = qkv.shape
+            q = rope_kv_append_ragged(qkv, positions, ctx.cos_table, ctx.sin_table, kc, vc,
+                                      self.active_base, self.active_cap, num_heads,
+                                      self.n_kv_heads)
         if ctx.decode:
             out = decode_attention_ragged(q.view(B, num_heads, D), kc, vc, ctx.seq_lens,
                                           self.active_base, self.active_cap, self.max_seq_len,

@@ -146,6 +146,44 @@ def test_wsgemm_swiglu_matches_rmsswiglu_oracle(fused, tokens, D, I):
     half_ulp_bar(out, ref, dtype, f"swiglu {tokens}x{D}x{I}")
 
 
+@pytest.mark.parametrize("splits", [2, 3, 4, 5, 7, 8])
+@pytest.mark.parametrize("epilogue,tokens,n,k", [
+    ("store", 32, 4096, 4096), ("residual", 64, 4096, 11008), ("store", 1, 300, 192),
+    ("residual", 17, 1000, 1088), ("swiglu", 40, 320, 512), ("store", 128, 640, 4096),
+    ("residual", 48, 384, 2048), ("swiglu", 80, 256, 1024), ("store", 112, 512, 960),
+])
+def test_wsgemm_split_k_cluster(monkeypatch, splits, epilogue, tokens, n, k):
+    """Split-k clusters (partial tiles reduce-scattered through distributed
+    shared memory); the split count is clamped to the k-blocks, to the shared
+    memory that holds a partial tile and to a divisor of the 4-token column
+    groups, so some cases run fewer splits."""
+    monkeypatch.setenv("LPC_WSGEMM_SPLITS", str(splits))
+    dtype = torch.bfloat16 if (splits + tokens) % 2 else torch.float16
+    g = torch.Generator().manual_seed(splits * 1000 + tokens + n)
+    x = (torch.randn(tokens, k, generator=g) * 0.5).to(dtype).to(DEV)
+    if epilogue == "swiglu":
+        gate = (torch.randn(n, k, generator=g) * k ** -0.5).to(dtype).to(DEV)
+        up = (torch.randn(n, k, generator=g) * k ** -0.5).to(dtype).to(DEV)
+        pw = PackedWeight(gate, up, layout="swiglu")
+        out = packed_linear(x, pw, "swiglu")
+        gf, uf = x.float() @ gate.float().t(), x.float() @ up.float().t()
+        ref = torch.nn.functional.silu(gf) * uf
+    else:
+        w = (torch.randn(n, k, generator=g) * k ** -0.5).to(dtype).to(DEV)
+        pw = PackedWeight(w)
+        ref = x.float() @ w.float().t()
+        if epilogue == "residual":
+            h = torch.randn(tokens, n, generator=g).to(dtype).to(DEV)
+            ref = ref + h.float()
+            out = packed_linear(x, pw, "residual", resid=h, out=h)
+        else:
+            out = packed_linear(x, pw)
+    half_ulp_bar(out, ref, dtype, f"split {splits} {epilogue} {tokens}x{n}x{k}")
+    if epilogue != "residual":
+        again = packed_linear(x, pw, epilogue)
+        assert torch.equal(out, again), "split-k reduction is not deterministic"
+
+
 def test_wsgemm_errors():
     w = PackedWeight(torch.randn(128, 64, device=DEV, dtype=torch.bfloat16))
     with pytest.raises(ValueError):
