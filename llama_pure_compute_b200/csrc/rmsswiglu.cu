@@ -18,18 +18,24 @@
 //                     (M=128, N=128, K=16 per instruction, fp32 accumulators)
 //          warps 0-3  epilogue: tcgen05.ld the gate and up columns of each token
 //                     row, silu(g)*u in fp32, one rounding to the output dtype
+//        (32 KB stages; tiles rasterised in groups of GROUP_M token tiles so
+//        that a wave of CTAs re-reads weight tiles from L2 rather than HBM)
 //      * a CTA pair (cluster of 2, tcgen05 cta_group::2) per 256-token x
-//        128-inter tile (more than 128 tokens): M = 256 tokens split over the
-//        two CTAs, N = 128 gate rows (CTA 0) + 128 up rows (CTA 1); both CTAs'
-//        TMA copies complete on CTA 0's barrier, CTA 0 issues the pair MMA and
-//        each CTA's TMEM ends up holding its own tokens' gate|up accumulators.
-//      smem rings of 32 KB stages with mbarrier full/empty handshakes; tiles
-//      rasterised in groups of GROUP_M token tiles so that a wave of CTAs
-//      re-reads weight tiles from L2 rather than HBM.
+//        w-inter tile (more than 128 tokens): M = 256 tokens split over the
+//        two CTAs; each CTA holds w/2 gate rows and w/2 up rows, CTA 0 issues
+//        one M=256, N=w MMA for gate and one for up, and each CTA's TMEM ends
+//        up holding its own tokens' gate|up accumulators.  Both CTAs' TMA
+//        copies complete on CTA 0's barrier.  The inter dimension is dealt out
+//        in 16-column units to a tile count matched to the number of CTA pairs
+//        per wave (69 tiles of 144/160 columns for the 7B layer: one wave at
+//        256 tokens, where 128-column tiles gave 86 pairs for 74 slots), and
+//        w is capped at 160 or 256 columns, whichever the load-time model of
+//        pair_tiles() finds faster for the token count.
 // fp32 path (CUDA cores, no TF32): each CTA normalises up to 8 token rows into
 //   shared memory, then streams gate/up rows with 16-byte loads and reduces the
 //   dot products per warp.  It is the weight-streaming (HBM-bound) GEMV of the
 //   fp32 op shape (8 tokens).
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 
@@ -228,26 +234,49 @@ __global__ void __launch_bounds__(192)
 // commits MMA completion to the empty / accumulator barriers of both CTAs.
 //   warps 0-3  epilogue (TMEM lane = token)
 // ---------------------------------------------------------------------------
-constexpr int PAIR_TOK = 256;     // tokens per pair tile
-constexpr int PAIR_I = 128;       // inter columns per pair tile
-constexpr int PAIR_STAGE = A_BYTES + PAIR_I * BK * 2;  // 16 KB tokens + 16 KB weights
+constexpr int PAIR_TOK = 256;  // tokens per pair tile (128 per CTA)
 
-template <int STAGES>
-constexpr int pair_smem() { return STAGES * PAIR_STAGE + 1024 + 256; }
+// WMAX: widest inter tile (gate + up = 2 x WMAX TMEM columns, <= 512).  Per
+// CTA and k-block a stage holds 128 token rows and WMAX/2 rows of each weight
+// (the TMA boxes), so WMAX sets the FLOPs per loaded byte: 160 for decode-
+// sized steps (69 tiles = one wave of the 74 pairs), 256 for larger ones.
+template <int WMAX>
+struct PairGeom {
+  static constexpr int BROWS = WMAX / 2;
+  static constexpr int B_BYTES = BROWS * BK * 2;  // a multiple of 1024
+  static constexpr int STAGE = A_BYTES + 2 * B_BYTES;
+};
 
-template <typename T, int STAGES>
+template <int WMAX, int STAGES>
+constexpr int pair_smem() { return STAGES * PairGeom<WMAX>::STAGE + 1024 + 256; }
+
+// Inter tile c of C covers columns [pair_col(c), pair_col(c + 1)): the I / 16
+// sixteen-column units dealt out as evenly as possible, so tile widths differ
+// by at most 16 and C can be matched to the number of CTA pairs per wave.
+__host__ __device__ __forceinline__ int pair_col(int c, int units, int C) {
+  return 16 * (int)(((int64_t)c * units) / C);
+}
+
+// CTA pair (cluster of 2, cta_group::2): one 256-token x w-column tile of
+// gate and up.  Rank r holds tokens m0 + 128r .. and weight rows
+// col0 + r*w/2 .. (w/2 gate rows, w/2 up rows) of each k-block; rank 0 issues
+// an M=256, N=w MMA for gate (TMEM columns 0..w-1) and one for up (columns
+// w..2w-1), each CTA receiving its own 128 token rows.
+template <typename T, int WMAX, int STAGES>
 __global__ void __launch_bounds__(192)
     swiglu_pair_kernel(const __grid_constant__ lpc::TmaDesc tmA,
                        const __grid_constant__ lpc::TmaDesc tmG,
                        const __grid_constant__ lpc::TmaDesc tmU, T* __restrict__ out, int M, int K,
-                       int I, int up_row_off, int num_m, int num_p, uint32_t idesc) {
-  constexpr uint32_t TMEM_COLS = 2 * PAIR_I;
+                       int I, int up_row_off, int num_m, int num_c, uint32_t ab_fmt) {
+  constexpr uint32_t TMEM_COLS = 512;
+  constexpr int PAIR_B_BYTES = PairGeom<WMAX>::B_BYTES;
+  constexpr int PAIR_STAGE = PairGeom<WMAX>::STAGE;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = lpc::smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;  // same offset in both CTAs of the pair
   const uint32_t sA = base;
-  const uint32_t sB = base + STAGES * A_BYTES;
-  const uint32_t bars = sB + STAGES * (PAIR_I * BK * 2);
+  const uint32_t sB = base + STAGES * A_BYTES;  // per stage: gate rows, then up rows
+  const uint32_t bars = sB + STAGES * (2 * PAIR_B_BYTES);
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
   const uint32_t accum_bar = bars + 8u * (2 * STAGES);
@@ -258,16 +287,16 @@ __global__ void __launch_bounds__(192)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = lpc::cluster_ctarank();
 
-  // grouped rasterisation over (token tile, inter tile) pairs
+  // consecutive pairs share an inter tile (its weights are read from HBM once
+  // and from L2 by the other token tiles)
   const int pid = blockIdx.x >> 1;
-  const int group = pid / (GROUP_M * num_p);
-  const int first_m = group * GROUP_M;
-  const int gm = min(GROUP_M, num_m - first_m);
-  const int within = pid - group * GROUP_M * num_p;
-  const int mt = first_m + within % gm;
-  const int pt = within / gm;
+  const int mt = pid % num_m;
+  const int ct = pid / num_m;
+  const int units = I / 16;
+  const int col0 = pair_col(ct, units, num_c);
+  const int w = pair_col(ct + 1, units, num_c) - col0;  // multiple of 16, <= WMAX
+  const int hw = w / 2;
   const int m0 = mt * PAIR_TOK + (int)rank * BM;  // this CTA's 128 tokens
-  const int i0 = pt * PAIR_I;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -279,7 +308,8 @@ __global__ void __launch_bounds__(192)
   }
   if (warp == 4 && lane == 0) {
     lpc::tma_prefetch_desc(&tmA);
-    lpc::tma_prefetch_desc(rank == 0 ? (const void*)&tmG : (const void*)&tmU);
+    lpc::tma_prefetch_desc(&tmG);
+    lpc::tma_prefetch_desc(&tmU);
   }
   lpc::cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrive
   if (warp == 5) {
@@ -295,23 +325,26 @@ __global__ void __launch_bounds__(192)
 
   if (warp == 4) {
     if (lane == 0) {
-      const lpc::TmaDesc* tw = rank == 0 ? &tmG : &tmU;
-      const int wrow = rank == 0 ? i0 : i0 + up_row_off;
+      const int grow = col0 + (int)rank * hw;
       // both CTAs' copies complete on rank 0's full barrier, armed by rank 0
-      // for the bytes of both halves
+      // for the bytes of both CTAs (every box is full size: rows past the
+      // matrix read as zeros and count)
       const uint32_t full0 = lpc::mapa_shared(full_bar(0), 0);
       for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % STAGES;
         const uint32_t r = (uint32_t)(kb / STAGES);
         if (!lpc::mbar_wait(empty_bar(s), (r & 1u) ^ 1u, st)) break;
         if (rank == 0) lpc::mbar_arrive_expect_tx(full_bar(s), 2 * PAIR_STAGE);
+        const uint32_t sb = sB + s * (2 * PAIR_B_BYTES);
         lpc::tma_load_2d_pair(sA + s * A_BYTES, &tmA, kb * BK, m0, full0 + 8u * s);
-        lpc::tma_load_2d_pair(sB + s * (PAIR_I * BK * 2), tw, kb * BK, wrow, full0 + 8u * s);
+        lpc::tma_load_2d_pair(sb, &tmG, kb * BK, grow, full0 + 8u * s);
+        lpc::tma_load_2d_pair(sb + PAIR_B_BYTES, &tmU, kb * BK, up_row_off + grow, full0 + 8u * s);
       }
     }
   } else if (warp == 5) {
     if (lane == 0) {
       if (rank == 0) {
+        const uint32_t idesc = lpc::idesc_f16(ab_fmt, PAIR_TOK, (uint32_t)w, 0u, 0u);
         const uint32_t peer_empty0 = lpc::mapa_shared(empty_bar(0), 1);
         const uint32_t peer_accum = lpc::mapa_shared(accum_bar, 1);
         for (int kb = 0; kb < nkb; ++kb) {
@@ -319,11 +352,15 @@ __global__ void __launch_bounds__(192)
           const uint32_t par = (uint32_t)(kb / STAGES) & 1u;
           if (!lpc::mbar_wait(full_bar(s), par, st)) break;
           lpc::tc_fence_after();
+          const uint32_t sb = sB + s * (2 * PAIR_B_BYTES);
           const uint64_t ad = lpc::smem_desc_sw128(sA + s * A_BYTES, 16, 1024);
-          const uint64_t bd = lpc::smem_desc_sw128(sB + s * (PAIR_I * BK * 2), 16, 1024);
+          const uint64_t gd = lpc::smem_desc_sw128(sb, 16, 1024);
+          const uint64_t ud = lpc::smem_desc_sw128(sb + PAIR_B_BYTES, 16, 1024);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            lpc::umma_ss_pair(tmem, ad + 2u * kk, bd + 2u * kk, idesc, (kb | kk) != 0);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            lpc::umma_ss_pair(tmem, ad + 2u * kk, gd + 2u * kk, idesc, (kb | kk) != 0);
+            lpc::umma_ss_pair(tmem + (uint32_t)w, ad + 2u * kk, ud + 2u * kk, idesc, (kb | kk) != 0);
+          }
           lpc::umma_commit_pair(empty_bar(s));
           lpc::umma_commit_pair(peer_empty0 + 8u * s);
         }
@@ -333,25 +370,25 @@ __global__ void __launch_bounds__(192)
     }
   } else {
     // epilogue warps 0..3: TMEM lanes 32*warp .. +31 = this CTA's tokens;
-    // columns 0..127 gate, 128..255 up, for inter columns i0 ..
+    // columns 0..w-1 gate, w..2w-1 up, for inter columns col0 ..
     const bool ok = lpc::mbar_wait(accum_bar, 0, st);
     lpc::tc_fence_after();
     if (ok) {
       const int row = m0 + warp * 32 + lane;
       const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
 #pragma unroll 1
-      for (int c = 0; c < PAIR_I; c += 16) {
+      for (int c = 0; c < w; c += 16) {
         uint32_t g[16], u[16];
         lpc::tmem_ld16(taddr + c, g);
-        lpc::tmem_ld16(taddr + PAIR_I + c, u);
+        lpc::tmem_ld16(taddr + w + c, u);
         lpc::tmem_wait_ld();
-        if (row < M && i0 + c < I) {
+        if (row < M && col0 + c < I) {
           uint32_t p[8];
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             p[j] = pack2<T>(silu_mul(__uint_as_float(g[2 * j]), __uint_as_float(u[2 * j])),
                             silu_mul(__uint_as_float(g[2 * j + 1]), __uint_as_float(u[2 * j + 1])));
-          uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)row * I + i0 + c);
+          uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)row * I + col0 + c);
           dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
           dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
         }
@@ -506,41 +543,72 @@ int launch_tc_cfg(const lpc::TmaDesc& ta, const lpc::TmaDesc& tg, const lpc::Tma
 
 // Tile shape by token count, measured on B200 for the 7B layer (dim 4096,
 // inter 11008) in steady state (launches back to back over weights larger
-// than L2):
-//   tokens        1-CTA 1x3   1-CTA 2x2   1-CTA 1x6   pair x3   pair x6
-//   32              44.2        63.3        53.8        55.4      61.6  us
-//   128             46.1        65.4        55.5        56.8      62.6
-//   256             69.8        69.1        74.2        59.5      65.3
-//   512             99.5       116.9       116.9        90.6      89.6
-//   2048           313.0       293.8       403.5       264.2     275.6
-// Up to 128 tokens the one-CTA tile with two ~96 KB CTAs per SM keeps every
-// weight tile streaming at once; beyond, the CTA pair halves the activation
-// bytes per weight byte (and the shared-memory operand traffic per MMA).
-// LPC_SWIGLU_CFG=1..5 forces a column of this table (measurement and tests).
+// than L2; each figure includes the row-norm launch), us:
+//   tokens   1-CTA 1x3   1-CTA 2x2   1-CTA 1x6   pair, 160-wide   pair, 256-wide
+//   128         46.3        66.4        55.1         48.2              --
+//   256         69.8        69.0        74.1         48.6             59.6
+//   1024       166.3       173.2       217.3        150.7            158.9
+//   2048       315.6       294.9       401.8        289.3            264.3
+//   4096       621.2       617.5       876.7        568.3            534.9
+// (the pair kernel with 128-column tiles, 86 pairs, took 59.6 / 153.1 / 266.2
+// / 519.9 at 256 / 1024 / 2048 / 4096 tokens.)  Up to 128 tokens the one-CTA
+// tile with two ~96 KB CTAs per SM keeps every weight tile streaming at once;
+// beyond, the CTA pair halves the activation bytes per weight byte (and the
+// shared-memory operand traffic per MMA).  LPC_SWIGLU_CFG=1..5 forces a
+// column of this table (measurement and tests).
 
-template <typename T, int STAGES>
+// Inter tiles for the pair kernel: the count C minimising the modelled time
+// waves x per-tile time, with one CTA pair per two SMs per wave (the kernel's
+// shared memory admits one CTA per SM).  A tile is bound by its loads (the
+// token rows and the full weight boxes per k-block, whatever its width):
+// measured on B200 at 2048-4096 tokens, about 1050 clocks per k-block with
+// 160-column boxes and 1540 with 256-column boxes, above the two MMAs (4
+// clocks per column).  Tiles are 128..wmax wide.  Returns the cost in clocks
+// per k-block.
+int64_t pair_tiles(int64_t num_m, int I, int wmax, int* num_c) {
+  const int64_t load = wmax <= 160 ? 1050 : 1540;
+  const int units = I / 16;
+  const int cmin = (units + wmax / 16 - 1) / (wmax / 16);
+  const int cmax = std::max(cmin, units / 8);  // widths >= 128
+  const int64_t per_wave = std::max(1, lpc::current_device_sms() / 2);
+  int best = cmin;
+  int64_t best_cost = -1;
+  for (int c = cmin; c <= cmax; ++c) {
+    const int64_t waves = (num_m * c + per_wave - 1) / per_wave;
+    const int64_t widest = 16 * ((units + c - 1) / c);
+    const int64_t cost = waves * std::max(load, 4 * widest);
+    if (best_cost < 0 || cost < best_cost) {
+      best = c;
+      best_cost = cost;
+    }
+  }
+  *num_c = best;
+  return best_cost;
+}
+
+template <typename T, int WMAX, int STAGES>
 int launch_pair(const lpc::TmaDesc& ta, const void* gw, const void* uw, void* out, int64_t M, int K,
                 int I, int dtype, cudaStream_t s) {
+  constexpr int BROWS = PairGeom<WMAX>::BROWS;
   lpc::TmaDesc tg, tu;
   int rc, up_off = 0;
   if (uw) {
-    if ((rc = lpc::make_tma_2d(&tg, gw, dtype, K, (uint64_t)I, (uint64_t)K * 2, BK, PAIR_I, true))) return rc;
-    if ((rc = lpc::make_tma_2d(&tu, uw, dtype, K, (uint64_t)I, (uint64_t)K * 2, BK, PAIR_I, true))) return rc;
+    if ((rc = lpc::make_tma_2d(&tg, gw, dtype, K, (uint64_t)I, (uint64_t)K * 2, BK, BROWS, true))) return rc;
+    if ((rc = lpc::make_tma_2d(&tu, uw, dtype, K, (uint64_t)I, (uint64_t)K * 2, BK, BROWS, true))) return rc;
   } else {
-    if ((rc = lpc::make_tma_2d(&tg, gw, dtype, K, (uint64_t)2 * I, (uint64_t)K * 2, BK, PAIR_I, true))) return rc;
+    if ((rc = lpc::make_tma_2d(&tg, gw, dtype, K, (uint64_t)2 * I, (uint64_t)K * 2, BK, BROWS, true))) return rc;
     tu = tg;
     up_off = I;
   }
-  constexpr int smem = pair_smem<STAGES>();
+  constexpr int smem = pair_smem<WMAX, STAGES>();
   static std::atomic<uint64_t> mask{0};
-  if ((rc = lpc::once_per_device_smem((const void*)swiglu_pair_kernel<T, STAGES>, smem, mask)))
+  if ((rc = lpc::once_per_device_smem((const void*)swiglu_pair_kernel<T, WMAX, STAGES>, smem, mask)))
     return rc;
   const int num_m = (int)((M + PAIR_TOK - 1) / PAIR_TOK);
-  const int num_p = (I + PAIR_I - 1) / PAIR_I;
-  const uint32_t idesc =
-      lpc::idesc_f16(dtype == LPC_DTYPE_BF16 ? 1u : 0u, PAIR_TOK, 2 * PAIR_I, 0u, 0u);
+  int num_c = 0;
+  pair_tiles(num_m, I, WMAX, &num_c);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(2 * (int64_t)num_m * num_p));
+  cfg.gridDim = dim3((unsigned)(2 * (int64_t)num_m * num_c));
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -551,13 +619,26 @@ int launch_pair(const lpc::TmaDesc& ta, const void* gw, const void* uw, void* ou
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, swiglu_pair_kernel<T, STAGES>, ta, tg, tu, (T*)out,
-                                     (int)M, K, I, up_off, num_m, num_p, idesc);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, swiglu_pair_kernel<T, WMAX, STAGES>, ta, tg, tu, (T*)out,
+                                     (int)M, K, I, up_off, num_m, num_c,
+                                     dtype == LPC_DTYPE_BF16 ? 1u : 0u);
   if (e != cudaSuccess) {
     lpc::set_error("rmsswiglu_forward (tcgen05 pair): launch failed: %s", cudaGetErrorString(e));
     return LPC_ERR_CUDA;
   }
   return lpc::check_launch("rmsswiglu_forward (tcgen05 pair)");
+}
+
+// The pair kernel with the cheaper of the 160- and 256-column tilings.
+template <typename T>
+int launch_pair_auto(const lpc::TmaDesc& ta, const void* gw, const void* uw, void* out, int64_t M,
+                     int K, int I, int dtype, cudaStream_t s) {
+  const int64_t num_m = (M + PAIR_TOK - 1) / PAIR_TOK;
+  int c160 = 0, c256 = 0;
+  const int64_t cost160 = pair_tiles(num_m, I, 160, &c160);
+  const int64_t cost256 = pair_tiles(num_m, I, 256, &c256);
+  if (cost256 < cost160) return launch_pair<T, 256, 4>(ta, gw, uw, out, M, K, I, dtype, s);
+  return launch_pair<T, 160, 5>(ta, gw, uw, out, M, K, I, dtype, s);
 }
 
 template <typename T>
@@ -580,10 +661,10 @@ int launch_tc(const void* xn, const void* gw, const void* uw, void* out, int64_t
   if (cfg == 1) return launch_tc_cfg<T, 1, 3>(ta, tg, tu, out, M, K, I, up_off, dtype, s);
   if (cfg == 2) return launch_tc_cfg<T, 2, 2>(ta, tg, tu, out, M, K, I, up_off, dtype, s);
   if (cfg == 3) return launch_tc_cfg<T, 1, 6>(ta, tg, tu, out, M, K, I, up_off, dtype, s);
-  if (cfg == 4) return launch_pair<T, 3>(ta, gw, uw, out, M, K, I, dtype, s);
-  if (cfg == 5) return launch_pair<T, 6>(ta, gw, uw, out, M, K, I, dtype, s);
+  if (cfg == 4) return launch_pair<T, 160, 5>(ta, gw, uw, out, M, K, I, dtype, s);
+  if (cfg == 5) return launch_pair<T, 256, 4>(ta, gw, uw, out, M, K, I, dtype, s);
   if (M <= 128) return launch_tc_cfg<T, 1, 3>(ta, tg, tu, out, M, K, I, up_off, dtype, s);
-  return launch_pair<T, 3>(ta, gw, uw, out, M, K, I, dtype, s);
+  return launch_pair_auto<T>(ta, gw, uw, out, M, K, I, dtype, s);
 }
 
 }  // namespace
