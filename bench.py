@@ -577,6 +577,38 @@ def run_ops(args):
                   "fused_op_us": round(us_op, 2),
                   "l2": "steady state over 6 weight sets (1.1 GB > L2)"})
         del ws, pws
+    if not only or "qkv_fused" in only:
+        from llama_pure_compute_b200.packed_linear import PackedWeight
+        # the attention block's projection + RoPE + KV append (one kernel on the
+        # packed q/k/v weight) against cuBLAS + lpc_rope_kv_append, steady state
+        # over 6 weight sets (604 MB > L2)
+        H = Hkv = 32
+        D, dim, R = 128, 4096, 6
+        g = torch.Generator(device=dev).manual_seed(11)
+        ws = [(0.02 * torch.randn((H + 2 * Hkv) * D, dim, device=dev, generator=g)).to(torch.bfloat16)
+              for _ in range(R)]
+        pws = [PackedWeight(w, layout="heads") for w in ws]
+        cos, sin = precompute_freqs_cis(D, 1024, device=dev)
+        cos, sin = cos.to(torch.bfloat16), sin.to(torch.bfloat16)
+        for M in (8, 16, 32):
+            x = torch.randn(M, 1, dim, device=dev, generator=g).to(torch.bfloat16)
+            pos = torch.randint(0, 1000, (M, 1), device=dev, generator=g)
+            kc = torch.zeros(M, Hkv, 1024, D, device=dev, dtype=torch.bfloat16)
+            vc = torch.zeros_like(kc)
+            us = _time_rotating([lambda pw=pw: ops.qkv_rope_append(x, pw, pos, cos, sin, kc, vc, H, Hkv)
+                                 for pw in pws])
+            us_two = _time_rotating([lambda w=w: ops.rope_kv_append(
+                torch.mm(x.view(M, dim), w.t()).view(M, 1, -1), pos, cos, sin, kc, vc, H, Hkv)
+                for w in ws])
+            byt = (H + 2 * Hkv) * D * dim * 2 + M * dim * 2 + M * (H + 2 * Hkv) * D * 2
+            emit({"op": f"qkv projection + RoPE + KV append 7B layer M={M} (packed heads)",
+                  "kernel": "wsgemm_kernel (EPI_QKV)", "us": round(us, 2), "bytes": byt,
+                  "achieved_gbs": round(byt / us / 1e3, 1), "peak_gbs": hbm,
+                  "frac": round(byt / us / 1e3 / hbm, 4), "bound": "hbm",
+                  "cublas_plus_rope_kv_append_us": round(us_two, 2),
+                  "l2": "steady state over 6 weight sets (604 MB > L2)"})
+            del kc, vc
+        del ws, pws
     if not only or "prefill" in only:
         torch.manual_seed(1)
         q, k, v = (torch.randn(4, 32, 2048, 128, device=dev).to(torch.bfloat16) for _ in range(3))
