@@ -38,6 +38,10 @@ __global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const T* __restrict__ 
                                                           T* __restrict__ y, int dim, float eps) {
   constexpr int PER = 16 / (int)sizeof(T);
   __shared__ float red[32];
+  // a dependent kernel launched with programmatic stream serialisation (the
+  // packed decode GEMM) may start its prologue and weight loads now; it waits
+  // for this grid to complete before it reads y
+  lpc::pdl_trigger();
   const int64_t row = blockIdx.x;
   const uint4* xr = reinterpret_cast<const uint4*>(x + row * dim);
   const int nvec = dim / PER;
@@ -76,6 +80,7 @@ __global__ void __launch_bounds__(256) rmsnorm_scalar_kernel(const T* __restrict
                                                              T* __restrict__ y, int dim,
                                                              float eps) {
   __shared__ float red[32];
+  lpc::pdl_trigger();  // as in rmsnorm_vec_kernel
   const int64_t row = blockIdx.x;
   const T* xr = x + row * dim;
   float ss = 0.f;
