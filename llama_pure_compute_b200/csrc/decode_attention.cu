@@ -338,6 +338,10 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const float* __restri
                                                           T* __restrict__ out, int H,
                                                           int max_splits, int64_t Smax,
                                                           KvRows rows) {
+  // the projection after attention, when launched with programmatic stream
+  // serialisation (the packed decode GEMM), may start its weight stream now;
+  // it waits for this grid to complete before reading `out`
+  lpc::pdl_trigger();
   const int64_t bh = blockIdx.x;
   const int64_t b = bh / H;
   int64_t row0;
