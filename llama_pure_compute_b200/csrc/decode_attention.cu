@@ -331,40 +331,77 @@ __global__ void __launch_bounds__((NCWARPS + 1) * 32)
   }
 }
 
+// One warp per (sequence, head): lane l merges output dims [l*D/32, (l+1)*D/32)
+// over the splits, in split order.  Up to CB splits every load is issued
+// before any is used (one memory round trip); longer sequences loop.
+constexpr int COMBINE_WARPS = 4;
 template <typename T, int D>
-__global__ void __launch_bounds__(D) decode_combine_kernel(const float* __restrict__ part_o,
-                                                          const float* __restrict__ part_ml,
-                                                          const int32_t* __restrict__ seq_lens,
-                                                          T* __restrict__ out, int H,
-                                                          int max_splits, int64_t Smax,
-                                                          KvRows rows) {
+__global__ void __launch_bounds__(COMBINE_WARPS * 32) decode_combine_kernel(
+    const float* __restrict__ part_o, const float* __restrict__ part_ml,
+    const int32_t* __restrict__ seq_lens, T* __restrict__ out, int H, int max_splits,
+    int64_t Smax, KvRows rows, int64_t bh_total) {
   // the projection after attention, when launched with programmatic stream
   // serialisation (the packed decode GEMM), may start its weight stream now;
   // it waits for this grid to complete before reading `out`
   lpc::pdl_trigger();
-  const int64_t bh = blockIdx.x;
+  constexpr int DPL = D / 32;
+  const int64_t bh = (int64_t)blockIdx.x * COMBINE_WARPS + (threadIdx.x >> 5);
+  if (bh >= bh_total) return;
+  const int lane = threadIdx.x & 31;
   const int64_t b = bh / H;
   int64_t row0;
   const int L = rows.length(b, 0, 1, Smax, __ldg(seq_lens + b), &row0, false);
-  const int d = threadIdx.x;
+  T* o = out + bh * D + lane * DPL;
   if (L <= 0) {
-    out[bh * D + d] = Num<T>::from_f(0.f);
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) o[i] = Num<T>::from_f(0.f);
     return;
   }
   const int ns = (L + CHUNK - 1) / CHUNK;
   if (ns <= 1) return;  // written by the split kernel
   const float* ml = part_ml + bh * max_splits * 2;
-  float M = -INFINITY;
-  for (int s = 0; s < ns; ++s) M = fmaxf(M, ml[2 * s]);
-  const float Mu = M == -INFINITY ? 0.f : M;
-  float O = 0.f, Ls = 0.f;
-  const float* po = part_o + bh * max_splits * D;
-  for (int s = 0; s < ns; ++s) {
-    const float f = fast_exp2(ml[2 * s] - Mu);
-    O = fmaf(f, po[s * D + d], O);
-    Ls = fmaf(f, ml[2 * s + 1], Ls);
+  const float* po = part_o + bh * max_splits * D + lane * DPL;
+  float O[DPL], Ls = 0.f;
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) O[i] = 0.f;
+  constexpr int CB = 8;
+  if (ns <= CB) {
+    float mv[CB], lv[CB], ov[CB][DPL];
+#pragma unroll
+    for (int k = 0; k < CB; ++k) {
+      const bool v = k < ns;
+      mv[k] = v ? ml[2 * k] : -INFINITY;
+      lv[k] = v ? ml[2 * k + 1] : 0.f;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) ov[k][i] = v ? po[k * D + i] : 0.f;
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < CB; ++k) M = fmaxf(M, mv[k]);
+    const float Mu = M == -INFINITY ? 0.f : M;
+#pragma unroll
+    for (int k = 0; k < CB; ++k) {
+      if (k < ns) {
+        const float f = fast_exp2(mv[k] - Mu);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) O[i] = fmaf(f, ov[k][i], O[i]);
+        Ls = fmaf(f, lv[k], Ls);
+      }
+    }
+  } else {
+    float M = -INFINITY;
+    for (int s = 0; s < ns; ++s) M = fmaxf(M, ml[2 * s]);
+    const float Mu = M == -INFINITY ? 0.f : M;
+    for (int s = 0; s < ns; ++s) {
+      const float f = fast_exp2(ml[2 * s] - Mu);
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) O[i] = fmaf(f, po[s * D + i], O[i]);
+      Ls = fmaf(f, ml[2 * s + 1], Ls);
+    }
   }
-  out[bh * D + d] = Num<T>::from_f(Ls > 0.f ? O / Ls : 0.f);
+  const float inv_ok = Ls > 0.f ? 1.f : 0.f;
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) o[i] = Num<T>::from_f(inv_ok > 0.f ? O[i] / Ls : 0.f);
 }
 
 template <typename T, int D, int G>
@@ -381,8 +418,10 @@ int launch_g(const void* q, const void* kc, const void* vc, const int32_t* lens,
       (const T*)q, (const T*)kc, (const T*)vc, lens, (T*)out, po, pml, H, Hkv, Smax, max_splits,
       scale_log2, rows);
   if ((rc = lpc::check_launch("decode_attention (split)"))) return rc;
-  decode_combine_kernel<T, D><<<(unsigned)(B * H), D, 0, s>>>(po, pml, lens, (T*)out, H,
-                                                              max_splits, Smax, rows);
+  const int64_t bh_total = B * (int64_t)H;
+  decode_combine_kernel<T, D>
+      <<<(unsigned)((bh_total + COMBINE_WARPS - 1) / COMBINE_WARPS), COMBINE_WARPS * 32, 0, s>>>(
+          po, pml, lens, (T*)out, H, max_splits, Smax, rows, bh_total);
   return lpc::check_launch("decode_attention (combine)");
 }
 
