@@ -10,23 +10,28 @@
 // 128-row tiles, head, batch), longest causal blocks first, dealt to the CTAs
 // in snake order; the next item's Q/K/V loads and first QK^T MMAs overlap the
 // current item's last tiles and epilogue (one CTA holds all 512 TMEM columns,
-// so consecutive CTAs on an SM could not overlap).  10 warps:
+// so consecutive CTAs on an SM could not overlap).  12 warps, 3 warpgroups;
+// warpgroup 2 (warps 8-11) gives registers to the two softmax warpgroups
+// (setmaxnreg: 96 and 200 per thread from the launch's 168):
 //   warp 8     TMA producer: Q0/Q1 once (64-column boxes), then K and V
 //              128-key tiles into 2-stage rings (4-D tensor maps: rows past
 //              kv_len / q_len read as zeros).  K/V tiles serve both Q tiles.
+//   warps 10-11 idle
 //   warp 9     TMEM allocator and single-thread tcgen05.mma issuer, per key tile j:
 //                S0 = Q0 K_j^T, S1 = Q1 K_j^T        (M=128, N=128, K=128)
 //                O0 += P0 V_j, O1 += P1 V_j          (A = P from TMEM, B = V, MN-major)
 //   warps 0-3  softmax for Q0, warps 4-7 softmax for Q1 (ping-pong: while one
 //              warpgroup exponentiates, the tensor core runs the other tile's
 //              MMAs).  Thread r of a warpgroup owns query row r (TMEM lane r):
-//              one tcgen05.ld of its 128 scores, row max and exp2 in fp32,
-//              P rounded to bf16/fp16 and stored back into the first 64
-//              columns of its own S buffer (two 16-bit values per column), the
-//              A operand of the PV MMA.  The running max moves (and O is
-//              rescaled in TMEM) only when a tile's max exceeds it by more
-//              than 2^8; the result is the same softmax, only the reference
-//              point of the exponentials differs.  Epilogue: O / l.
+//              one tcgen05.ld of its 128 scores, exp2 in fp32 against the
+//              running max straight away while the tile's row max is reduced
+//              alongside, P rounded to bf16/fp16 and stored back into the
+//              first 64 columns of its own S buffer (two 16-bit values per
+//              column), the A operand of the PV MMA.  The running max moves
+//              (the row's exponentials are redone from S, still in TMEM, and
+//              O is rescaled) only when a tile's max exceeds it by more than
+//              2^8; the result is the same softmax, only the reference point
+//              of the exponentials differs.  Epilogue: O / l.
 // TMEM (512 columns): S0/P0 [0,128), S1/P1 [128,256), O0 [256,384), O1 [384,512).
 // MMAs issued by one thread execute in order, so S_t of key tile j+1 never
 // overwrites P_t of tile j before PV_t(j) has read it.
@@ -60,7 +65,7 @@ constexpr int TILE_BYTES = BQ * HD * 2;   // 32 KB: one Q tile, one K or V stage
 constexpr int HALF_BYTES = TILE_BYTES / 2;
 constexpr int KV_STAGES = 2;
 constexpr int SMEM_BYTES = (NQT + 2 * KV_STAGES) * TILE_BYTES + 1024 + 256;
-constexpr int NTHREADS = 320;
+constexpr int NTHREADS = 384;  // 2 softmax warpgroups + 1 load/MMA warpgroup
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
@@ -160,6 +165,11 @@ __device__ __forceinline__ int item_of(int c, int G, int r) {
   return r * G + ((r & 1) ? (G - 1 - c) : c);
 }
 
+constexpr int LAUNCH_REGS = 168;  // the register split below assumes this count
+constexpr int SPLIT_REGS_LOADMMA = 96, SPLIT_REGS_SOFTMAX = 200;
+static_assert(128 * SPLIT_REGS_LOADMMA + 256 * SPLIT_REGS_SOFTMAX <= NTHREADS * LAUNCH_REGS,
+              "register split exceeds the block's launch allocation");
+
 template <typename T>
 __global__ void __launch_bounds__(NTHREADS, 1)
     flash_prefill_kernel(const __grid_constant__ TmaDesc4 tmQ, const __grid_constant__ TmaDesc4 tmK,
@@ -222,6 +232,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t tmem = *tmem_slot_ptr;
   unsigned int* st = &g_prefill_status;
 
+  if (warp >= 8) {
+  // Register split: warpgroup 2 (load, MMA, two idle warps) hands registers to
+  // the softmax warpgroups.  At the launch's 168 registers per thread the
+  // shares fit the block's total: 128 x 96 + 256 x 200 <= 384 x 168 (the host
+  // refuses to launch with any other count).
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 96;\n" ::: "memory");
   if (warp == 8) {
     // ---------------- TMA producer ----------------
     // Q of the next item as soon as the last S MMA of the previous one is
@@ -331,7 +347,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         c1 += (uint32_t)it.n1;
       }
     }
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 200;\n" ::: "memory");
     // ---------------- softmax + epilogue: warpgroup t = warp / 4 ----------------
     const int t = warp >> 2;
     const int rr = (warp & 3) * 32 + lane;         // row within the query tile = TMEM lane
@@ -360,17 +378,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const bool need_mask = (k0 + BKV > p.kv_len) ||
                                (p.causal && k0 + BKV - 1 > p.offset + it.q0 + (int64_t)t * BQ);
         uint32_t sv[BKV];
+        auto load_s = [&]() {
 #pragma unroll
-        for (int cc = 0; cc < BKV; cc += 32)
-          lpc::tmem_ld32(tS + cc, *reinterpret_cast<uint32_t(*)[32]>(&sv[cc]));
-        lpc::tmem_wait_ld();
-        if (need_mask) {
-          // keys k0 + i with i > lim - k0 are invisible to this row
-          const int lim_rel = (int)max((int64_t)-1, min(lim - k0, (int64_t)(BKV - 1)));
+          for (int cc = 0; cc < BKV; cc += 32)
+            lpc::tmem_ld32(tS + cc, *reinterpret_cast<uint32_t(*)[32]>(&sv[cc]));
+          lpc::tmem_wait_ld();
+          if (need_mask) {
+            // keys k0 + i with i > lim - k0 are invisible to this row
+            const int lim_rel = (int)max((int64_t)-1, min(lim - k0, (int64_t)(BKV - 1)));
 #pragma unroll
-          for (int q = 0; q < BKV; ++q)
-            if (q > lim_rel) sv[q] = 0xff800000u;  // -inf
-        }
+            for (int q = 0; q < BKV; ++q)
+              if (q > lim_rel) sv[q] = 0xff800000u;  // -inf
+          }
+        };
+        load_s();
         // row max: four independent chains of 3-input max
         float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
@@ -381,33 +402,43 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           m3 = max3(m3, __uint_as_float(sv[q + 6]), __uint_as_float(sv[q + 7]));
         }
         const float mt = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * p.scale_log2;  // scale > 0
+        // tile 0 sets the reference max; later tiles exponentiate against the
+        // running one straight away (their max is reduced alongside) and redo
+        // the row only if its max grew by more than the threshold
+        if (j == 0) m_used = mt;
+        const uint64_t sc2 = pack_f2(p.scale_log2, p.scale_log2);
+        uint64_t rsa = 0, rsb = 0;
+        uint32_t pk[BKV / 2];
+        auto exps = [&](float m_ref) {
+          const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+          const uint64_t nm2 = pack_f2(-m_use, -m_use);
+          rsa = 0;
+          rsb = 0;
+#pragma unroll
+          for (int q = 0; q < BKV; q += 2) {
+            const uint64_t x = fma_f2(pack_u2(sv[q], sv[q + 1]), sc2, nm2);
+            const uint64_t e = pack_f2(fast_exp2(lo_f(x)), fast_exp2(hi_f(x)));
+            if ((q >> 1) & 1) rsb = add_f2(rsb, e);
+            else rsa = add_f2(rsa, e);
+            pk[q >> 1] = pack2<T>(lo_f(e), hi_f(e));
+          }
+        };
+        exps(m_used);
+        float alpha = 1.f;
+        bool rescale = false;
+        const bool grow = j > 0 && mt > m_used + RESCALE_THRESHOLD;
+        if (__any_sync(0xffffffffu, grow)) {  // warp-uniform: tcgen05.ld is warp-collective
+          if (grow) {
+            alpha = fast_exp2(m_used - mt);
+            m_used = mt;
+            rescale = true;
+          }
+          load_s();  // S is still in TMEM: the redo does not keep the row live
+          exps(m_used);  // rows whose max did not grow recompute the same values
+        }
         // PV_t(j-1) must be done: its P shares these TMEM columns and O must be stable
         if (j >= 1 && !wait_warp(o_done(t), (ph - 1u) & 1u)) { ok = false; break; }
         lpc::tc_fence_after();
-        float alpha = 1.f;
-        bool rescale = false;
-        if (j == 0) {
-          m_used = mt;
-        } else if (mt > m_used + RESCALE_THRESHOLD) {
-          alpha = fast_exp2(m_used - mt);
-          m_used = mt;
-          rescale = true;
-        }
-        const float m_use = m_used == -INFINITY ? 0.f : m_used;
-        // e = exp2(s * scale - m), two at a time (packed fma, packed row-sum
-        // adds on two chains), all 128 before the TMEM stores.
-        const uint64_t sc2 = pack_f2(p.scale_log2, p.scale_log2);
-        const uint64_t nm2 = pack_f2(-m_use, -m_use);
-        uint64_t rsa = 0, rsb = 0;
-        uint32_t pk[BKV / 2];
-#pragma unroll
-        for (int q = 0; q < BKV; q += 2) {
-          const uint64_t x = fma_f2(pack_u2(sv[q], sv[q + 1]), sc2, nm2);
-          const uint64_t e = pack_f2(fast_exp2(lo_f(x)), fast_exp2(hi_f(x)));
-          if ((q >> 1) & 1) rsb = add_f2(rsb, e);
-          else rsa = add_f2(rsa, e);
-          pk[q >> 1] = pack2<T>(lo_f(e), hi_f(e));
-        }
 #pragma unroll
         for (int cc = 0; cc < BKV / 2; cc += 16)
           lpc::tmem_st16(tS + (uint32_t)cc, *reinterpret_cast<uint32_t(*)[16]>(&pk[cc]));
@@ -549,6 +580,24 @@ extern "C" int lpc_flash_attention(const void* q, const void* k, const void* v, 
   // persistent: one CTA per SM loops over the work items
   dim3 grid((unsigned)std::min<int64_t>(items, current_device_sms()));
   int rc;
+  // the kernel's setmaxnreg split is sized for LAUNCH_REGS registers per thread:
+  // with fewer, the softmax warpgroups' increase could never be granted
+  {
+    static int regs[2] = {0, 0};
+    const int ti = dtype == LPC_DTYPE_BF16 ? 0 : 1;
+    if (regs[ti] == 0) {
+      cudaFuncAttributes fa;
+      const cudaError_t e = dtype == LPC_DTYPE_BF16
+                                ? cudaFuncGetAttributes(&fa, flash_prefill_kernel<__nv_bfloat16>)
+                                : cudaFuncGetAttributes(&fa, flash_prefill_kernel<__half>);
+      regs[ti] = e == cudaSuccess ? fa.numRegs : -1;
+    }
+    if (regs[ti] != LAUNCH_REGS) {
+      set_error("flash_attention: kernel built with %d registers per thread, its register split "
+                "needs %d", regs[ti], LAUNCH_REGS);
+      return LPC_ERR_UNSUPPORTED;
+    }
+  }
   if (dtype == LPC_DTYPE_BF16) {
     static std::atomic<uint64_t> mask{0};
     if ((rc = once_per_device_smem((const void*)flash_prefill_kernel<__nv_bfloat16>, SMEM_BYTES, mask)))
