@@ -116,53 +116,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
   }
 }
 
-// Bounded wait with cluster-scope acquire: data that other CTAs of the
-// cluster wrote before their release-arrive on `bar` is visible afterwards.
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0u;
-}
-__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
-                                                  unsigned int* status) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((it & 255u) == 0u && global_timer_ns() - t0 > LPC_WAIT_LIMIT_NS) {
-      atomicOr(status, LPC_DEV_ERR_TIMEOUT);
-      return false;
-    }
-  }
-}
-
-// Bounded wait that polls with test_wait (never suspends the thread): for a
-// single issuing thread whose wake-up latency is on the critical path.
-__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, unsigned int* status) {
-  const uint64_t t0 = global_timer_ns();
-  for (uint32_t it = 0;; ++it) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (ok) return true;
-    if ((it & 1023u) == 1023u && global_timer_ns() - t0 > LPC_WAIT_LIMIT_NS) {
-      atomicOr(status, LPC_DEV_ERR_TIMEOUT);
-      return false;
-    }
-  }
-}
-
 // 1-D bulk copy global -> shared, completion signalled as tx bytes on `bar`.
 // Both addresses 16-byte aligned, size a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
@@ -257,11 +210,6 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
 }
-// Arrive on an mbarrier of another CTA of the cluster (address from mapa_shared).
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
-}
 // 2-D tiled TMA load by either CTA of a pair into its own shared memory, with
 // the transaction bytes counted on `bar_cluster` -- an mbarrier of the pair's
 // rank-0 CTA (its address from mapa_shared).  No multicast.
@@ -285,13 +233,6 @@ __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// Split cluster barrier: every thread of every CTA arrives once, then waits once.
-__device__ __forceinline__ void cluster_arrive_relaxed() {
-  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() {
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
                    "memory");
