@@ -22,6 +22,18 @@ def test_shard_partitions_global_batch():
     assert bench.shard(256, 8, 7) == (224, 32)
 
 
+def test_lpt_partition_of_the_long_context_prompts():
+    """Long-context run: LPT over prompt + new tokens covers every sequence
+    once, and no rank exceeds another by more than the heaviest sequence."""
+    lens = [len(p) + bench.LONG_NEW for p in bench.long_prompts()]
+    assert len(lens) == bench.LONG_SEQS
+    for world in (1, 2, 4, 8):
+        parts, loads = bench.lpt_partition(lens, world)
+        assert sorted(i for part in parts for i in part) == list(range(len(lens)))
+        assert [sum(lens[i] for i in part) for part in parts] == loads
+        assert max(loads) - min(loads) <= max(lens)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
