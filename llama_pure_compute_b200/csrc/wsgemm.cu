@@ -15,14 +15,21 @@
 //     a pipeline stage is 16 KB of weights plus NT * 128 bytes of
 //     activations, and two ~100 KB CTAs fit per SM, so a layer with up to
 //     ~300 weight tiles keeps every tile streaming at once.
-//   * One CTA per weight tile, the whole K.  Layers with few tiles (tens)
-//     leave SMs idle: this kernel is meant for the wide projections.
+//   * One CTA per weight tile over the whole K when there are enough tiles;
+//     layers with few tiles split K over clusters of up to 8 CTAs whose fp32
+//     partial tiles are reduce-scattered through distributed shared memory.
+//   * Launched with programmatic stream serialisation: the first weight
+//     chunks stream in under the previous kernel on the stream.
 // Measured on B200 in steady state (launches back to back over weights larger
-// than L2), SwiGLU gate/up of the 7B layer (2 x 11008 x 4096): 33.6 us at 32
-// tokens, 35.3 us at 64, 41.8 us at 128 -- against 44-46 us for the
-// activation-major tile of the fused rmsswiglu op on the raw weights.
-// Epilogues: plain store, residual add (out = resid + acc, may alias), and
-// SwiGLU on weights packed with 16 gate rows / 16 up rows interleaved.
+// than L2), SwiGLU gate/up of the 7B layer (2 x 11008 x 4096): 30.0 us at 32
+// tokens, 32.4 us at 64, 38.9 us at 128 -- against 44-46 us for the
+// activation-major tile of the fused rmsswiglu op on the raw weights; the
+// q/k/v projection with RoPE and KV append (EPI_QKV): 21.2 / 21.5 / 23.0 us
+// at 8 / 16 / 32 tokens against 24.7 / 26.8 / 27.0 for cuBLAS followed by
+// lpc_rope_kv_append.
+// Epilogues: plain store, residual add (out = resid + acc, may alias), SwiGLU
+// on weights packed with 16 gate rows / 16 up rows interleaved, and EPI_QKV on
+// the "heads" packing.
 //   warp 0    producer: bulk copy of the weight chunk + TMA box of activations
 //   warp 2    TMEM allocator + single-thread tcgen05.mma issuer
 //   warps 4-7 epilogue (TMEM lane = weight row)
