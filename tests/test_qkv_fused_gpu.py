@@ -65,7 +65,7 @@ def test_pack_heads_layout_bit_exact():
     assert np.array_equal(pw.data.cpu().numpy().view(np.uint16), pack_ref(tile_order_heads(_u16(w))))
 
 
-@pytest.mark.parametrize("splits", [None, "1", "2", "4"])
+@pytest.mark.parametrize("splits", [None, "1", "2", "3", "4"])
 @pytest.mark.parametrize("B,S,H,Hkv,dim,dtype", [
     (32, 1, 8, 8, 512, torch.bfloat16), (5, 1, 8, 2, 256, torch.bfloat16),
     (3, 4, 4, 4, 320, torch.float16), (64, 1, 4, 1, 1024, torch.bfloat16),
