@@ -322,6 +322,7 @@ __global__ void __launch_bounds__(192)
   const uint32_t tmem = *tmem_slot_ptr;
   const int nkb = K / BK;
   unsigned int* st = &g_swiglu_status;
+  if (warp != 4) lpc::pdl_wait();
 
   if (warp == 4) {
     if (lane == 0) {
@@ -330,15 +331,29 @@ __global__ void __launch_bounds__(192)
       // for the bytes of both CTAs (every box is full size: rows past the
       // matrix read as zeros and count)
       const uint32_t full0 = lpc::mapa_shared(full_bar(0), 0);
-      for (int kb = 0; kb < nkb; ++kb) {
+      auto load_w = [&](int kb) {
         const int s = kb % STAGES;
-        const uint32_t r = (uint32_t)(kb / STAGES);
-        if (!lpc::mbar_wait(empty_bar(s), (r & 1u) ^ 1u, st)) break;
         if (rank == 0) lpc::mbar_arrive_expect_tx(full_bar(s), 2 * PAIR_STAGE);
         const uint32_t sb = sB + s * (2 * PAIR_B_BYTES);
-        lpc::tma_load_2d_pair(sA + s * A_BYTES, &tmA, kb * BK, m0, full0 + 8u * s);
         lpc::tma_load_2d_pair(sb, &tmG, kb * BK, grow, full0 + 8u * s);
         lpc::tma_load_2d_pair(sb + PAIR_B_BYTES, &tmU, kb * BK, up_row_off + grow, full0 + 8u * s);
+      };
+      auto load_a = [&](int kb) {
+        const int s = kb % STAGES;
+        lpc::tma_load_2d_pair(sA + s * A_BYTES, &tmA, kb * BK, m0, full0 + 8u * s);
+      };
+      // The gate/up weights are never written by the kernel this one may
+      // overlap (the row norm of the same call): the first ring of weight
+      // boxes needs no empty-slot wait and is issued before waiting on it.
+      const int first = nkb < STAGES ? nkb : STAGES;
+      for (int kb = 0; kb < first; ++kb) load_w(kb);
+      lpc::pdl_wait();  // the normalised activations come from the previous kernel
+      for (int kb = 0; kb < first; ++kb) load_a(kb);
+      for (int kb = first; kb < nkb; ++kb) {
+        const uint32_t r = (uint32_t)(kb / STAGES);
+        if (!lpc::mbar_wait(empty_bar(kb % STAGES), (r & 1u) ^ 1u, st)) break;
+        load_w(kb);
+        load_a(kb);
       }
     }
   } else if (warp == 5) {
@@ -612,13 +627,17 @@ int launch_pair(const lpc::TmaDesc& ta, const void* gw, const void* uw, void* ou
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  // programmatic stream serialisation: the set-up and the first weight boxes
+  // overlap the row norm launched just before by this call
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, swiglu_pair_kernel<T, WMAX, STAGES>, ta, tg, tu, (T*)out,
                                      (int)M, K, I, up_off, num_m, num_c,
                                      dtype == LPC_DTYPE_BF16 ? 1u : 0u);
