@@ -24,14 +24,15 @@
 //              warpgroup exponentiates, the tensor core runs the other tile's
 //              MMAs).  Thread r of a warpgroup owns query row r (TMEM lane r):
 //              one tcgen05.ld of its 128 scores, exp2 in fp32 against the
-//              running max straight away while the tile's row max is reduced
-//              alongside, P rounded to bf16/fp16 and stored back into the
-//              first 64 columns of its own S buffer (two 16-bit values per
-//              column), the A operand of the PV MMA.  The running max moves
-//              (the row's exponentials are redone from S, still in TMEM, and
-//              O is rescaled) only when a tile's max exceeds it by more than
-//              2^8; the result is the same softmax, only the reference point
-//              of the exponentials differs.  Epilogue: O / l.
+//              running max straight away (only the first key tile of an item
+//              reduces its row max), P rounded to bf16/fp16 and stored back
+//              into the first 64 columns of its own S buffer (two 16-bit
+//              values per column), the A operand of the PV MMA.  A row sum
+//              above 2^8 is the only sign that the max may have grown by more
+//              than 8 (log2 units); such warps reduce the tile's max, move the
+//              running max, redo the row's exponentials from S (still in
+//              TMEM) and rescale O.  The result is the same softmax, only the
+//              reference point of the exponentials differs.  Epilogue: O / l.
 // TMEM (512 columns): S0/P0 [0,128), S1/P1 [128,256), O0 [256,384), O1 [384,512).
 // MMAs issued by one thread execute in order, so S_t of key tile j+1 never
 // overwrites P_t of tile j before PV_t(j) has read it.
@@ -68,7 +69,9 @@ constexpr int SMEM_BYTES = (NQT + 2 * KV_STAGES) * TILE_BYTES + 1024 + 256;
 constexpr int NTHREADS = 384;  // 2 softmax warpgroups + 1 load/MMA warpgroup
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float LOG2E = 1.4426950408889634f;
-constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+// A row whose max grew by more than 8 (log2 units) past its reference has a
+// row sum above 2^8: such rows reduce their max and redo the tile.
+constexpr float RESCALE_LIMIT = 256.0f;
 
 struct TmaDesc4 { alignas(64) unsigned char bytes[128]; };
 
@@ -378,44 +381,42 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const bool need_mask = (k0 + BKV > p.kv_len) ||
                                (p.causal && k0 + BKV - 1 > p.offset + it.q0 + (int64_t)t * BQ);
         uint32_t sv[BKV];
+        const int lim_rel = (int)max((int64_t)-1, min(lim - k0, (int64_t)(BKV - 1)));
+        // keys k0 + i with i > lim_rel are invisible to this row
+        auto mask_part = [&](int q0, int q1) {
+          if (need_mask) {
+#pragma unroll
+            for (int q = 0; q < BKV; ++q)
+              if (q >= q0 && q < q1 && q > lim_rel) sv[q] = 0xff800000u;  // -inf
+          }
+        };
         auto load_s = [&]() {
 #pragma unroll
           for (int cc = 0; cc < BKV; cc += 32)
             lpc::tmem_ld32(tS + cc, *reinterpret_cast<uint32_t(*)[32]>(&sv[cc]));
           lpc::tmem_wait_ld();
-          if (need_mask) {
-            // keys k0 + i with i > lim - k0 are invisible to this row
-            const int lim_rel = (int)max((int64_t)-1, min(lim - k0, (int64_t)(BKV - 1)));
-#pragma unroll
-            for (int q = 0; q < BKV; ++q)
-              if (q > lim_rel) sv[q] = 0xff800000u;  // -inf
-          }
+          mask_part(0, BKV);
         };
-        load_s();
-        // row max: four independent chains of 3-input max
-        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+        auto row_max = [&]() {  // four independent chains of 3-input max
+          float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-        for (int q = 0; q < BKV; q += 8) {
-          m0 = max3(m0, __uint_as_float(sv[q]), __uint_as_float(sv[q + 1]));
-          m1 = max3(m1, __uint_as_float(sv[q + 2]), __uint_as_float(sv[q + 3]));
-          m2 = max3(m2, __uint_as_float(sv[q + 4]), __uint_as_float(sv[q + 5]));
-          m3 = max3(m3, __uint_as_float(sv[q + 6]), __uint_as_float(sv[q + 7]));
-        }
-        const float mt = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * p.scale_log2;  // scale > 0
-        // tile 0 sets the reference max; later tiles exponentiate against the
-        // running one straight away (their max is reduced alongside) and redo
-        // the row only if its max grew by more than the threshold
-        if (j == 0) m_used = mt;
+          for (int q = 0; q < BKV; q += 8) {
+            m0 = max3(m0, __uint_as_float(sv[q]), __uint_as_float(sv[q + 1]));
+            m1 = max3(m1, __uint_as_float(sv[q + 2]), __uint_as_float(sv[q + 3]));
+            m2 = max3(m2, __uint_as_float(sv[q + 4]), __uint_as_float(sv[q + 5]));
+            m3 = max3(m3, __uint_as_float(sv[q + 6]), __uint_as_float(sv[q + 7]));
+          }
+          return fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * p.scale_log2;  // scale > 0
+        };
         const uint64_t sc2 = pack_f2(p.scale_log2, p.scale_log2);
         uint64_t rsa = 0, rsb = 0;
         uint32_t pk[BKV / 2];
-        auto exps = [&](float m_ref) {
+        auto exps_part = [&](float m_ref, int q0, int q1) {
           const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
           const uint64_t nm2 = pack_f2(-m_use, -m_use);
-          rsa = 0;
-          rsb = 0;
 #pragma unroll
           for (int q = 0; q < BKV; q += 2) {
+            if (q < q0 || q >= q1) continue;
             const uint64_t x = fma_f2(pack_u2(sv[q], sv[q + 1]), sc2, nm2);
             const uint64_t e = pack_f2(fast_exp2(lo_f(x)), fast_exp2(hi_f(x)));
             if ((q >> 1) & 1) rsb = add_f2(rsb, e);
@@ -423,18 +424,33 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             pk[q >> 1] = pack2<T>(lo_f(e), hi_f(e));
           }
         };
-        exps(m_used);
+        // Tile 0 sets the reference max.  Later tiles exponentiate against
+        // the running one without reducing their own max: a row whose max
+        // grew by more than the threshold has an exponential, hence a row
+        // sum, above 2^threshold, and only such warps reduce the max and redo.
+        load_s();
+        if (j == 0) m_used = row_max();
+        exps_part(m_used, 0, BKV);
         float alpha = 1.f;
         bool rescale = false;
-        const bool grow = j > 0 && mt > m_used + RESCALE_THRESHOLD;
-        if (__any_sync(0xffffffffu, grow)) {  // warp-uniform: tcgen05.ld is warp-collective
-          if (grow) {
-            alpha = fast_exp2(m_used - mt);
-            m_used = mt;
-            rescale = true;
+        {
+          const uint64_t rs2 = add_f2(rsa, rsb);
+          const float rs = lo_f(rs2) + hi_f(rs2);
+          // also a row with no reference yet (all keys so far masked) that now sees a key
+          const bool big = j > 0 && (!(rs <= RESCALE_LIMIT) || (m_used == -INFINITY && rs > 0.f));
+          if (__any_sync(0xffffffffu, big)) {  // warp-uniform: tcgen05.ld is warp-collective
+            load_s();  // S is still in TMEM
+            if (big) {
+              const float mt = row_max();
+              if (mt > m_used) {
+                alpha = fast_exp2(m_used - mt);
+                m_used = mt;
+                rescale = true;
+              }
+            }
+            rsa = rsb = 0;
+            exps_part(m_used, 0, BKV);  // rows that kept their max recompute the same values
           }
-          load_s();  // S is still in TMEM: the redo does not keep the row live
-          exps(m_used);  // rows whose max did not grow recompute the same values
         }
         // PV_t(j-1) must be done: its P shares these TMEM columns and O must be stable
         if (j >= 1 && !wait_warp(o_done(t), (ph - 1u) & 1u)) { ok = false; break; }
@@ -443,8 +459,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int cc = 0; cc < BKV / 2; cc += 16)
           lpc::tmem_st16(tS + (uint32_t)cc, *reinterpret_cast<uint32_t(*)[16]>(&pk[cc]));
         const uint64_t rs2 = add_f2(rsa, rsb);
-        const float rs = lo_f(rs2) + hi_f(rs2);
-        l = l * alpha + rs;
+        l = l * alpha + (lo_f(rs2) + hi_f(rs2));
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
           for (int cc = 0; cc < HD; cc += 16) {

@@ -323,6 +323,33 @@ def test_flash_prefill(B, H, S, causal):
     torch.testing.assert_close(o.float(), ref, rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("profile", ["plateau", "ramp", "drop"])
+@pytest.mark.parametrize("causal", [True, False])
+def test_flash_prefill_running_max_moves(profile, causal):
+    """Scores whose row max moves across key tiles: later tiles a little above
+    tile 0 everywhere (row sums of a tile far above 2^8 with the max grown by
+    about 3 in log2 units), rising without bound (max grows by more than 8
+    per tile), or far below tile 0."""
+    B, H, S, D = 1, 2, 1024, 128
+    g = torch.Generator(device=DEV).manual_seed(7)
+    u = torch.ones(D, device=DEV) / math.sqrt(D)
+    pos = torch.arange(S, device=DEV, dtype=torch.float32)
+    if profile == "plateau":
+        b = torch.where(pos < 128, 1.0, 2.5)
+    elif profile == "ramp":
+        b = 1.0 + pos / 32.0
+    else:
+        b = torch.where(pos < 128, 4.0, 0.25)
+    noise = lambda s: s * torch.randn(B, H, S, D, device=DEV, generator=g)
+    q = (16.0 * u + noise(0.05)).to(torch.bfloat16)
+    k = (b[None, None, :, None] * u + noise(0.05)).to(torch.bfloat16)
+    v = torch.randn(B, H, S, D, device=DEV, generator=g).to(torch.bfloat16)
+    o = flash_attention_v2(q, k, v, causal=causal)
+    ref = attention_ref(q, k, v, causal=causal).float()
+    assert torch.isfinite(o.float()).all()
+    assert (o.float() - ref).abs().max().item() <= 2e-2
+
+
 def test_flash_prefill_op_shape():
     """Prefill op shape: Q,K,V [4, 32, 2048, 128] ~N(0,1) bf16, causal, scale 1/sqrt(128), seed 1."""
     torch.manual_seed(1)
