@@ -19,7 +19,8 @@
 //   warps 10-11 idle
 //   warp 9     TMEM allocator and single-thread tcgen05.mma issuer, per key tile j:
 //                S0 = Q0 K_j^T, S1 = Q1 K_j^T        (M=128, N=128, K=128)
-//                O0 += P0 V_j, O1 += P1 V_j          (A = P from TMEM, B = V, MN-major)
+//                O0 += P0 V_j, O1 += P1 V_j          (A = P from TMEM, B = V, MN-major;
+//                                                     keys 0-63 as soon as their P is stored)
 //   warps 0-3  softmax for Q0, warps 4-7 softmax for Q1 (ping-pong: while one
 //              warpgroup exponentiates, the tensor core runs the other tile's
 //              MMAs).  Thread r of a warpgroup owns query row r (TMEM lane r):
@@ -27,12 +28,16 @@
 //              running max straight away (only the first key tile of an item
 //              reduces its row max), P rounded to bf16/fp16 and stored back
 //              into the first 64 columns of its own S buffer (two 16-bit
-//              values per column), the A operand of the PV MMA.  A row sum
-//              above 2^8 is the only sign that the max may have grown by more
-//              than 8 (log2 units); such warps reduce the tile's max, move the
+//              values per column), the A operand of the PV MMA.  P of the
+//              first 64 keys is released (its own barrier) before the last 64
+//              are exponentiated, so half of PV overlaps them.  Before that
+//              release a warp checks for a max grown by more than 8 (log2
+//              units): a first-half row sum above 2^8, or the second half's
+//              max.  Such warps (rare) reduce the tile's max, move the
 //              running max, redo the row's exponentials from S (still in
-//              TMEM) and rescale O.  The result is the same softmax, only the
-//              reference point of the exponentials differs.  Epilogue: O / l.
+//              TMEM), rescale O and release all of P at once.  The result is
+//              the same softmax, only the reference point of the exponentials
+//              differs.  Epilogue: O / l.
 // TMEM (512 columns): S0/P0 [0,128), S1/P1 [128,256), O0 [256,384), O1 [384,512).
 // MMAs issued by one thread execute in order, so S_t of key tile j+1 never
 // overwrites P_t of tile j before PV_t(j) has read it.
@@ -195,6 +200,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   auto p_full = [&](int t) { return bars + 8u * (11 + t); };
   auto o_done = [&](int t) { return bars + 8u * (13 + t); };
   auto o_free = [&](int t) { return bars + 8u * (15 + t); };  // epilogue has read O_t
+  auto p_half = [&](int t) { return bars + 8u * (17 + t); };  // P_t of the first 64 keys stored
   const uint32_t tmem_slot = bars + 8u * 20;
   volatile uint32_t* tmem_slot_ptr =
       reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
@@ -215,6 +221,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     for (int t = 0; t < NQT; ++t) {
       lpc::mbar_init(s_full(t), 1);
       lpc::mbar_init(p_full(t), 4);
+      lpc::mbar_init(p_half(t), 4);
       lpc::mbar_init(o_done(t), 1);
       lpc::mbar_init(o_free(t), 4);
     }
@@ -305,12 +312,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       };
       auto issue_pv = [&](int t, uint32_t kv, uint32_t pc, bool first) -> bool {
         const int s = kv % KV_STAGES;
-        if (!lpc::mbar_wait(p_full(t), pc & 1u, st)) return false;
+        // the first 64 keys' P is released before the softmax exponentiates
+        // the other 64: their MMAs overlap it
+        if (!lpc::mbar_wait(p_half(t), pc & 1u, st)) return false;
         if (!lpc::mbar_wait(v_full(s), (kv / KV_STAGES) & 1u, st)) return false;
         lpc::tc_fence_after();
         const uint64_t bv = dV + (uint64_t)((s * TILE_BYTES) >> 4);
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk) {
+          if (kk == BKV / 32) {
+            if (!lpc::mbar_wait(p_full(t), pc & 1u, st)) return false;
+            lpc::tc_fence_after();
+          }
           // A: P_t in TMEM (16 keys = 8 columns of packed pairs); B: V rows = keys
           lpc::umma_ts(tmem + 256u + 128u * t, tmem + 128u * t + 8u * kk,
                        bv + (uint64_t)((kk * 16 * 128) >> 4), idesc_pv, (!first) || kk != 0);
@@ -429,52 +442,88 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // grew by more than the threshold has an exponential, hence a row
         // sum, above 2^threshold, and only such warps reduce the max and redo.
         load_s();
-        if (j == 0) m_used = row_max();
-        exps_part(m_used, 0, BKV);
-        float alpha = 1.f;
-        bool rescale = false;
-        {
-          const uint64_t rs2 = add_f2(rsa, rsb);
-          const float rs = lo_f(rs2) + hi_f(rs2);
-          // also a row with no reference yet (all keys so far masked) that now sees a key
-          const bool big = j > 0 && (!(rs <= RESCALE_LIMIT) || (m_used == -INFINITY && rs > 0.f));
-          if (__any_sync(0xffffffffu, big)) {  // warp-uniform: tcgen05.ld is warp-collective
-            load_s();  // S is still in TMEM
-            if (big) {
-              const float mt = row_max();
-              if (mt > m_used) {
-                alpha = fast_exp2(m_used - mt);
-                m_used = mt;
-                rescale = true;
-              }
-            }
-            rsa = rsb = 0;
-            exps_part(m_used, 0, BKV);  // rows that kept their max recompute the same values
+        // the last 64 keys' max, in log2 units: a growth past the threshold
+        // there must be known before the first 64 keys' P is released
+        float mt_hi = -INFINITY;
+        if (j == 0) {
+          m_used = row_max();
+        } else {
+          float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+          for (int q = BKV / 2; q < BKV; q += 4) {
+            m0 = max3(m0, __uint_as_float(sv[q]), __uint_as_float(sv[q + 1]));
+            m1 = max3(m1, __uint_as_float(sv[q + 2]), __uint_as_float(sv[q + 3]));
           }
+          mt_hi = fmaxf(m0, m1) * p.scale_log2;
         }
+        exps_part(m_used, 0, BKV / 2);
+        const uint64_t rs_lo2 = add_f2(rsa, rsb);
+        const float rs_lo = lo_f(rs_lo2) + hi_f(rs_lo2);
+        // a grown max: a first-half row sum above 2^8, a second-half max more
+        // than 8 above the reference, or a first visible key
+        const bool big = j > 0 && (!(rs_lo <= RESCALE_LIMIT) || !(mt_hi <= m_used + 8.f) ||
+                                   (m_used == -INFINITY && rs_lo > 0.f));
         // PV_t(j-1) must be done: its P shares these TMEM columns and O must be stable
         if (j >= 1 && !wait_warp(o_done(t), (ph - 1u) & 1u)) { ok = false; break; }
         lpc::tc_fence_after();
-#pragma unroll
-        for (int cc = 0; cc < BKV / 2; cc += 16)
-          lpc::tmem_st16(tS + (uint32_t)cc, *reinterpret_cast<uint32_t(*)[16]>(&pk[cc]));
-        const uint64_t rs2 = add_f2(rsa, rsb);
-        l = l * alpha + (lo_f(rs2) + hi_f(rs2));
-        if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll 1
-          for (int cc = 0; cc < HD; cc += 16) {
-            uint32_t v[16];
-            lpc::tmem_ld16(tO + cc, v);
-            lpc::tmem_wait_ld();
-#pragma unroll
-            for (int q = 0; q < 16; ++q) v[q] = __float_as_uint(__uint_as_float(v[q]) * alpha);
-            lpc::tmem_st16(tO + cc, v);
+        if (__any_sync(0xffffffffu, big)) {  // warp-uniform: tcgen05.ld is warp-collective
+          // rare: new reference max for the whole row, O rescaled, all of P
+          // stored before either half is released
+          float alpha = 1.f;
+          bool rescale = false;
+          load_s();  // S is still in TMEM (no P stored yet)
+          if (big) {
+            const float mt = row_max();
+            if (mt > m_used) {
+              alpha = fast_exp2(m_used - mt);
+              m_used = mt;
+              rescale = true;
+            }
           }
+          rsa = rsb = 0;
+          exps_part(m_used, 0, BKV);  // rows that kept their max recompute the same values
+#pragma unroll
+          for (int cc = 0; cc < BKV / 2; cc += 16)
+            lpc::tmem_st16(tS + (uint32_t)cc, *reinterpret_cast<uint32_t(*)[16]>(&pk[cc]));
+          const uint64_t rs2 = add_f2(rsa, rsb);
+          l = l * alpha + (lo_f(rs2) + hi_f(rs2));
+          if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+            for (int cc = 0; cc < HD; cc += 16) {
+              uint32_t v[16];
+              lpc::tmem_ld16(tO + cc, v);
+              lpc::tmem_wait_ld();
+#pragma unroll
+              for (int q = 0; q < 16; ++q) v[q] = __float_as_uint(__uint_as_float(v[q]) * alpha);
+              lpc::tmem_st16(tO + cc, v);
+            }
+          }
+          lpc::tmem_wait_st();
+          lpc::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            lpc::mbar_arrive(p_half(t));
+            lpc::mbar_arrive(p_full(t));
+          }
+        } else {
+#pragma unroll
+          for (int cc = 0; cc < BKV / 4; cc += 16)
+            lpc::tmem_st16(tS + (uint32_t)cc, *reinterpret_cast<uint32_t(*)[16]>(&pk[cc]));
+          lpc::tmem_wait_st();
+          lpc::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) lpc::mbar_arrive(p_half(t));
+          exps_part(m_used, BKV / 2, BKV);
+#pragma unroll
+          for (int cc = BKV / 4; cc < BKV / 2; cc += 16)
+            lpc::tmem_st16(tS + (uint32_t)cc, *reinterpret_cast<uint32_t(*)[16]>(&pk[cc]));
+          const uint64_t rs2 = add_f2(rsa, rsb);
+          l += lo_f(rs2) + hi_f(rs2);
+          lpc::tmem_wait_st();
+          lpc::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) lpc::mbar_arrive(p_full(t));
         }
-        lpc::tmem_wait_st();
-        lpc::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) lpc::mbar_arrive(p_full(t));
       }
       // epilogue: O / l, then O_t is free for the next item's PV
       if (ok && (ok = wait_warp(o_done(t), (cnt + (uint32_t)n - 1u) & 1u))) {
