@@ -264,6 +264,41 @@ def test_rmsswiglu_op_shape_bf16_distribution():
                  "rmsswiglu bf16 op shape")
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_rmsswiglu_zero_large_ranks_and_repeatability(dtype):
+    """As tests/test_rmsswiglu_correctness.py:174-263 of the reference: 1-D /
+    2-D / 3-D inputs, all-zero rows (exact zeros out), inputs scaled by 1e3
+    (the norm removes the scale), and bit-identical repeated calls (the split
+    and pair reductions have a fixed order)."""
+    g = torch.Generator(device=DEV).manual_seed(11)
+    D, I = 1024, 640
+    w = (1 + 0.02 * torch.randn(D, device=DEV, generator=g)).to(dtype)
+    gw = (torch.randn(I, D, device=DEV, generator=g) / D ** 0.5).to(dtype)
+    uw = (torch.randn(I, D, device=DEV, generator=g) / D ** 0.5).to(dtype)
+    x = torch.randn(2, 160, D, device=DEV, generator=g).to(dtype)
+    x[0, 5] = 0
+    x[1, 77] = 0
+    tol = (lambda y, r, what: torch.testing.assert_close(y, r, rtol=1e-5, atol=1e-5)) \
+        if dtype == torch.float32 else (lambda y, r, what: half_ulp_bar(y, r, dtype, what))
+    rnd = dtype != torch.float32
+    y3 = ops.rmsswiglu_forward(x, w, gw, uw, 1e-6)
+    assert y3.shape == (2, 160, I)
+    tol(y3, rmsswiglu_ref(x, w, gw, uw, 1e-6, round_normed=rnd), "rmsswiglu 3-D")
+    assert (y3[0, 5] == 0).all() and (y3[1, 77] == 0).all()
+    y2 = ops.rmsswiglu_forward(x.reshape(-1, D), w, gw, uw, 1e-6)
+    assert y2.shape == (320, I) and torch.equal(y2, y3.reshape(-1, I))
+    y1 = ops.rmsswiglu_forward(x[1, 3], w, gw, uw, 1e-6)
+    assert y1.shape == (I,)
+    tol(y1, rmsswiglu_ref(x[1, 3:4], w, gw, uw, 1e-6, round_normed=rnd)[0], "rmsswiglu 1-D")
+    big = (x.float() * 1e3).to(dtype)
+    yb = ops.rmsswiglu_forward(big, w, gw, uw, 1e-6)
+    assert torch.isfinite(yb.float()).all()
+    tol(yb, rmsswiglu_ref(big, w, gw, uw, 1e-6, round_normed=rnd), "rmsswiglu x1e3")
+    for xx in (x, x[:, :4]):
+        assert torch.equal(ops.rmsswiglu_forward(xx, w, gw, uw, 1e-6),
+                           ops.rmsswiglu_forward(xx, w, gw, uw, 1e-6))
+
+
 @pytest.mark.parametrize("M", [1, 3, 127, 129, 300])
 def test_rmsswiglu_ragged_token_counts(M):
     g = torch.Generator(device=DEV).manual_seed(M)
