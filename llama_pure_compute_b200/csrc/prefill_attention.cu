@@ -74,8 +74,10 @@ constexpr int SMEM_BYTES = (NQT + 2 * KV_STAGES) * TILE_BYTES + 1024 + 256;
 constexpr int NTHREADS = 384;  // 2 softmax warpgroups + 1 load/MMA warpgroup
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float LOG2E = 1.4426950408889634f;
-// A row whose max grew by more than 8 (log2 units) past its reference has a
-// row sum above 2^8: such rows reduce their max and redo the tile.
+// A row whose max grew by more than RESCALE_LOG2 (log2 units) past its
+// reference has a row sum above RESCALE_LIMIT = 2^RESCALE_LOG2: such rows
+// reduce their max and redo the tile.
+constexpr float RESCALE_LOG2 = 8.0f;
 constexpr float RESCALE_LIMIT = 256.0f;
 
 struct TmaDesc4 { alignas(64) unsigned char bytes[128]; };
@@ -461,7 +463,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const float rs_lo = lo_f(rs_lo2) + hi_f(rs_lo2);
         // a grown max: a first-half row sum above 2^8, a second-half max more
         // than 8 above the reference, or a first visible key
-        const bool big = j > 0 && (!(rs_lo <= RESCALE_LIMIT) || !(mt_hi <= m_used + 8.f) ||
+        const bool big = j > 0 && (!(rs_lo <= RESCALE_LIMIT) || !(mt_hi <= m_used + RESCALE_LOG2) ||
                                    (m_used == -INFINITY && rs_lo > 0.f));
         // PV_t(j-1) must be done: its P shares these TMEM columns and O must be stable
         if (j >= 1 && !wait_warp(o_done(t), (ph - 1u) & 1u)) { ok = false; break; }
