@@ -45,9 +45,9 @@ PROMPT_LEN = 512
 NEW_TOKENS = 128
 SEED = 3
 # ncu dram bytes (read + write) / algorithmic bytes of the decode-attention
-# kernel, from one capture of the ragged 16-sequence case
-# (profiles/decode_attention_ragged16.md): 589.1 MB / 583.9 MB.  The bench
-# scales it to its own launch (traffic grows with the K/V bytes processed).
+# kernel, from one dram__bytes capture of a 16-sequence ragged launch (589.1 MB
+# of traffic for 583.9 MB of K/V, q and output).  The bench scales it to its
+# own launch (traffic grows with the K/V bytes processed).
 DECODE_ATTN_TRAFFIC_RATIO = (583.322880e6 + 5.812224e6) / 583.942144e6
 
 
@@ -69,6 +69,10 @@ def parse():
                     help="decode: the 7B decode workload (default); ops: per-op roofline lines; "
                          "longctx: 64 prompts of 1k-8k tokens, prefill + 256 decode steps")
     ap.add_argument("--only", default="", help="comma list of op lines for --suite ops")
+    ap.add_argument("--no-kernels", action="store_true",
+                    help="skip the per-kernel roofline block of the decode line")
+    ap.add_argument("--no-longctx", action="store_true",
+                    help="skip the long-context block of the decode line")
     ap.add_argument("--decode-batch", type=int, default=64,
                     help="sequences of the ragged decode op line (64 = the decode op shape)")
     return ap.parse_args()
@@ -125,6 +129,17 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(under) if under else None,
                 "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
                 "samples": len(sm)}
+
+
+def smi_index(local: int) -> int:
+    """nvidia-smi index of this process's GPU (CUDA_VISIBLE_DEVICES remaps it)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            return int(vis.split(",")[local])
+        except (ValueError, IndexError):
+            pass
+    return local
 
 
 # ---------------------------------------------------------------------------
@@ -306,8 +321,7 @@ def run_ours(args, world, rank, local):
     dec.capture()  # runs the step body twice: one eager warm-up, one captured
     launches_per_step = (_lib.launch_count - n0) // 2
 
-    clocks = ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else
-                          int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local]))
+    clocks = ClockSampler(smi_index(local))
     clocks.start()
     for _ in range(pre_steps):  # untimed warm-up steps (also move to the mean context)
         dec.step()
@@ -366,6 +380,9 @@ def run_ours(args, world, rank, local):
     wall_e2e = max_over_ranks((time.perf_counter() - w0) * 1e3, world)
     e2e_tok_s = args.batch * e_steps / (e2e_ms / 1e3)
     clk = clocks.stop()
+    # device-side error flags (bounded waits that gave up, bounds checks) of
+    # every kernel run so far: a run with any flag set is not a measurement
+    status = int(max_over_ranks(float(_lib.device_status()), world))
 
     # ---- dominant kernel: split-KV decode attention, timed standalone on the
     # final decode state (layer 0 cache, current per-sequence lengths) ----
@@ -403,7 +420,20 @@ def run_ours(args, world, rank, local):
     mean_ctx_timed = ctx_first + (args.steps + 1) / 2
     kv_bytes = int(B * mean_ctx_timed) * cfg.num_layers * 2 * cfg.num_kv_heads * cfg.head_dim * 2
     step_bytes = weight_bytes + kv_bytes
+    n_layers = cfg.num_layers
     dec.release()
+    del dec, model, kv, q, outb, ws
+    torch.cuda.empty_cache()
+
+    kernels = None
+    if not args.no_kernels:
+        kernels = measure_kernels(dev)
+        status = max(status, int(max_over_ranks(float(_lib.device_status()), world)))
+    longctx = None
+    if not args.no_longctx and args.layers == 32:
+        torch.cuda.empty_cache()
+        longctx = longctx_measure(args, world, rank, local)
+        status = max(status, int(longctx.get("device_status", 0)))
 
     if rank == 0:
         cpu = None
@@ -416,7 +446,8 @@ def run_ours(args, world, rank, local):
             "unit": UNIT,
             "n_gpus": world,
             "steps": args.steps,
-            "warmup": pre_steps,
+            "warmup": args.warmup,
+            "pre_steps": pre_steps,
             "ms_per_step": round(ms_max / args.steps, 3),
             "higher_is_better": True,
             "scaling": "strong",
@@ -433,7 +464,9 @@ def run_ours(args, world, rank, local):
                 "context_timed": [ctx_first, ctx_first + args.steps - 1],
                 "parallelism": f"sequence-sharded replicas x{world} (no collective)",
                 "l2": "inputs larger than L2 (each step streams ~13 GB weights + KV cache)",
-                "layers": cfg.num_layers,
+                "layers": n_layers,
+                "pre_steps": "untimed decode steps before the timed ones (the first `warmup` of "
+                             "them are the warm-up; all move the context to the timed window)",
             },
             "clocks": clk,
             "e2e": {"value": round(e2e_tok_s, 1), "unit": UNIT, "h2d_bytes_per_step": 2 * 8 * B,
@@ -448,8 +481,8 @@ def run_ours(args, world, rank, local):
                 "unit": "GB/s",
                 "frac": round(attn_gbs / hbm_peak, 4),
                 "traffic": int(attn_bytes * DECODE_ATTN_TRAFFIC_RATIO),
-                "traffic_source": "ncu capture of the 16-sequence ragged case scaled by bytes "
-                                  "(profiles/decode_attention_ragged16.md)",
+                "traffic_source": "ncu dram__bytes of a 16-sequence ragged decode-attention "
+                                  "launch, scaled by the K/V bytes of this launch",
                 "algorithmic_bytes_per_launch": attn_bytes,
                 "launch_us": round(attn_us, 2),
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (burst)" if peaks else "fallback 6650",
@@ -463,8 +496,157 @@ def run_ours(args, world, rank, local):
                         "ms": round(prefill_ms, 1),
                         "tok_s": round(args.batch * args.prompt_len / (prefill_ms / 1e3), 1)},
             "cpu_baseline": cpu,
+            "device_status": status,
+            "kernels": kernels,
+            "longctx": longctx,
         }
         print(json.dumps(line), flush=True)
+    if status:
+        print(f"device status {status:#x}: a kernel flagged a timeout or a bounds failure; "
+              "the numbers above are not valid", file=sys.stderr, flush=True)
+        raise SystemExit(3)
+
+
+# ---------------------------------------------------------------------------
+# per-kernel rooflines in the decode line (same run, CUDA events)
+# ---------------------------------------------------------------------------
+def _kentry(kernel, shape, us, *, nbytes=None, flops=None, hbm, tc, timing):
+    d = {"kernel": kernel, "shape": shape, "us": round(us, 2), "timing": timing}
+    if nbytes is not None:
+        d["bytes"] = int(nbytes)
+        d["achieved_gbs"] = round(nbytes / us / 1e3, 1)
+        d["frac_hbm"] = round(nbytes / us / 1e3 / hbm, 4)
+    if flops is not None:
+        d["flops"] = int(flops)
+        d["tflops"] = round(flops / us / 1e6, 1)
+        d["frac_tc"] = round(flops / us / 1e6 / tc, 4)
+    return d
+
+
+def measure_kernels(dev):
+    """Device time of each hot-path kernel at its benchmark shape, with the
+    algorithmic bytes / FLOPs of one launch and the fraction of the measured
+    peaks (HBM copy GB/s; dense bf16 TF/s, burst).  Weight-streaming kernels are
+    timed in steady state, launches back to back over distinct weights whose
+    total exceeds L2 (what a decode step does); the others over inputs larger
+    than L2, or rotated over several input sets whose total exceeds it."""
+    from llama_pure_compute_b200 import ops
+    from llama_pure_compute_b200.flash_attention import flash_attention_v2
+    from llama_pure_compute_b200.model import precompute_freqs_cis
+    from llama_pure_compute_b200.packed_linear import PackedWeight, packed_linear
+    pk = _peaks()
+    hbm = pk.get("hbm_gbs", 6650.0)
+    tc = pk.get("bf16_tflops", 1590.0)
+    bf = torch.bfloat16
+    D, I, H = 4096, 11008, 32
+    out = []
+    steady = "steady state: back to back over distinct weight sets (> L2)"
+    rot = "back to back over distinct input sets (> L2 in total)"
+    g = torch.Generator(device=dev).manual_seed(5)
+
+    def rn(*shape, std=1.0, dtype=bf):
+        return (std * torch.randn(*shape, device=dev, generator=g)).to(dtype)
+
+    with torch.inference_mode():
+        # SwiGLU of the 7B layer at 256 tokens: row norm + CTA-pair tcgen05 GEMM
+        M = 256
+        x = rn(M, D)
+        w1 = torch.ones(D, device=dev, dtype=bf)
+        ws = [rn(2 * I, D, std=0.02) for _ in range(6)]
+        empty = torch.empty(0, device=dev, dtype=bf)
+        us = _time_rotating([lambda w=w: ops.rmsswiglu_forward(x, w1, w, empty, 1e-5) for w in ws])
+        out.append(_kentry("rmsnorm_vec_kernel + swiglu_pair_kernel", "7B gate/up, 256 tokens", us,
+                           nbytes=2 * I * D * 2 + M * D * 2 + M * I * 2, flops=2 * M * D * 2 * I,
+                           hbm=hbm, tc=tc, timing=steady))
+        # decode-sized SwiGLU on packed weights (32 tokens)
+        pws = [PackedWeight(w, layout="swiglu") for w in ws]
+        M = 32
+        x = rn(M, D)
+        us = _time_rotating([lambda pw=pw: packed_linear(x, pw, "swiglu") for pw in pws])
+        out.append(_kentry("wsgemm_kernel (SwiGLU epilogue)", "7B gate/up, 32 tokens", us,
+                           nbytes=2 * I * D * 2 + M * D * 2 + M * I * 2, hbm=hbm, tc=tc,
+                           timing=steady))
+        del ws, pws
+        # q/k/v projection + RoPE + KV append (32 tokens)
+        wq = [rn(3 * H * 128, D, std=0.02) for _ in range(6)]
+        pq = [PackedWeight(w, layout="heads") for w in wq]
+        cos, sin = precompute_freqs_cis(128, 1024, device=dev)
+        cos, sin = cos.to(bf), sin.to(bf)
+        x = rn(M, 1, D)
+        pos = torch.randint(0, 1000, (M, 1), device=dev, generator=g)
+        kc = torch.zeros(M, H, 1024, 128, device=dev, dtype=bf)
+        vc = torch.zeros_like(kc)
+        us = _time_rotating([lambda pw=pw: ops.qkv_rope_append(x, pw, pos, cos, sin, kc, vc, H, H)
+                             for pw in pq])
+        out.append(_kentry("wsgemm_kernel (EPI_QKV: projection + RoPE + KV append)",
+                           "7B q/k/v, 32 tokens", us,
+                           nbytes=3 * H * 128 * D * 2 + M * D * 2 + M * 3 * H * 128 * 2, hbm=hbm,
+                           tc=tc, timing=steady))
+        del wq, pq, kc, vc
+        # prefill attention [4, 32, 2048, 128] causal
+        q, k, v = (rn(4, 32, 2048, 128) for _ in range(3))
+        us = _time_us(lambda: flash_attention_v2(q, k, v, causal=True, sm_scale=128 ** -0.5), 10)
+        out.append(_kentry("flash_prefill_kernel", "[4, 32, 2048, 128] causal", us,
+                           nbytes=4 * 4 * 32 * 2048 * 128 * 2,
+                           flops=2 * 4 * 32 * 2048 * 2048 * 128, hbm=hbm, tc=tc,
+                           timing="inputs 201 MB (> L2), launches back to back"))
+        del q, k, v
+        # fp32 RMSNorm + SwiGLU op shape (x [8, 4096], W 2 x [11008, 4096] fp32)
+        xf = rn(8, D, dtype=torch.float32)
+        wf = 1 + 0.02 * torch.randn(D, device=dev, generator=g)
+        gu = [(rn(I, D, std=0.02, dtype=torch.float32), rn(I, D, std=0.02, dtype=torch.float32))
+              for _ in range(2)]
+        us = _time_rotating([lambda a=a, b=b: ops.rmsswiglu_forward(xf, wf, a, b, 1e-6)
+                             for a, b in gu])
+        out.append(_kentry("swiglu_f32_kernel", "fp32 op: x [8, 4096], W 2 x [11008, 4096]", us,
+                           nbytes=(2 * I * D + 8 * D + D + 8 * I) * 4, hbm=hbm, tc=tc,
+                           timing=steady))
+        del gu
+        # RoPE + KV append at a prefill size: 4 x 2048 tokens
+        B, S = 4, 2048
+        sets = []
+        cos, sin = precompute_freqs_cis(128, S, device=dev)
+        cos, sin = cos.to(bf), sin.to(bf)
+        posp = torch.arange(S, device=dev).unsqueeze(0).expand(B, -1).contiguous()
+        for _ in range(3):
+            sets.append((rn(B, S, 3 * H * 128), torch.empty(B, H, S, 128, device=dev, dtype=bf),
+                         torch.empty(B, H, S, 128, device=dev, dtype=bf),
+                         torch.empty(B, H, S, 128, device=dev, dtype=bf),
+                         rn(B * S, H, 128), rn(B * S, H, 128)))
+        us = _time_rotating([lambda t=t: ops.rope_kv_append(t[0], posp, cos, sin, t[1], t[2], H, H,
+                                                            q_out=t[3]) for t in sets])
+        out.append(_kentry("rope_kv_append_kernel", "4 x 2048 tokens, 32 + 2 x 32 heads", us,
+                           nbytes=2 * B * S * 3 * H * 128 * 2, hbm=hbm, tc=tc, timing=rot))
+        # KV append alone (update_kv_cache) at the same size
+        us = _time_rotating([lambda t=t: ops.update_kv_cache(t[4], t[5], t[1], t[2]) for t in sets])
+        out.append(_kentry("kv_append_kernel", "8192 tokens x 32 heads x 128 (K and V)", us,
+                           nbytes=2 * 2 * B * S * H * 128 * 2, hbm=hbm, tc=tc, timing=rot))
+        del sets
+        # row RMSNorm at 8192 x 4096
+        xs = [rn(B * S, D) for _ in range(4)]
+        us = _time_rotating([lambda t=t: ops.rmsnorm_forward(t, w1, 1e-5) for t in xs])
+        out.append(_kentry("rmsnorm_vec_kernel", "8192 x 4096", us,
+                           nbytes=2 * B * S * D * 2 + D * 2, hbm=hbm, tc=tc, timing=rot))
+        del xs
+        # decode attention at the decode op shape: 64 sequences, L ~ U[128, 4096]
+        torch.manual_seed(2)
+        L = torch.randint(128, 4097, (64,))
+        Smax = 4097
+        kc = rn(64, H, Smax, 128)
+        vc = rn(64, H, Smax, 128)
+        qd = rn(64, H, 128)
+        lens = (L + 1).to(torch.int32).to(dev)
+        wsd = ops.decode_attention_workspace(64, H, Smax, 128, dev)
+        od = torch.empty_like(qd)
+        us = _time_us(lambda: ops.decode_attention(qd, kc, vc, lens, None, od, wsd), 10)
+        out.append(_kentry("decode_split_kernel + decode_combine_kernel",
+                           "64 sequences, L ~ U[128, 4096], 32 heads x 128", us,
+                           nbytes=int((L + 1).sum()) * H * 128 * 2 * 2 + 2 * 64 * H * 128 * 2,
+                           hbm=hbm, tc=tc, timing="4.3 GB cache (> L2), launches back to back"))
+        del kc, vc
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -695,6 +877,16 @@ def lpt_partition(weights, world):
 
 
 def run_longctx(args, world, rank, local):
+    line = longctx_measure(args, world, rank, local)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if line.get("device_status"):
+        raise SystemExit(3)
+
+
+def longctx_measure(args, world, rank, local):
+    """The long-context mixed run on this rank's LPT share; every rank takes
+    the same collective steps and returns the same line."""
     from llama_pure_compute_b200 import _lib
     from llama_pure_compute_b200.generate import BatchedGreedyDecoder
     from llama_pure_compute_b200.model import LlamaForCausalLM
@@ -719,7 +911,7 @@ def run_longctx(args, world, rank, local):
     dec = BatchedGreedyDecoder(model, cache, len(mine), use_cuda_graph=True, prefill_chunk=1)
 
     barrier(world)
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(smi_index(local))
     clocks.start()
     p0 = torch.cuda.Event(enable_timing=True)
     p1 = torch.cuda.Event(enable_timing=True)
@@ -739,8 +931,11 @@ def run_longctx(args, world, rank, local):
     barrier(world)
     decode_ms = max_over_ranks(d0.elapsed_time(d1), world)
     clk = clocks.stop()
-    status = _lib.device_status()
+    status = int(max_over_ranks(float(_lib.device_status()), world))
+    kv_gb = round(cache.memory_footprint_bytes() / 1e9, 2)
     dec.release()
+    del dec, cache, model
+    torch.cuda.empty_cache()
 
     sum_p = sum(lens)
     prefill_flops = 2 * 6.476e9 * sum_p + 2 * 32 * 128 * 32 * sum(n * n for n in lens)
@@ -763,7 +958,7 @@ def run_longctx(args, world, rank, local):
                                "256 greedy decode steps, ragged KV cache",
                    "sum_prompt_tokens": sum_p, "prompt_len_min": min(lens),
                    "prompt_len_max": max(lens), "partition": "LPT on prompt+256",
-                   "rank_loads": loads, "kv_cache_gb_rank0": round(cache.memory_footprint_bytes() / 1e9, 2),
+                   "rank_loads": loads, "kv_cache_gb_rank0": kv_gb,
                    "packed_swiglu": packed},
         "prefill": {"tokens": sum_p, "ms": round(prefill_ms, 1),
                     "tok_s": round(sum_p / (prefill_ms / 1e3), 1),
@@ -777,8 +972,7 @@ def run_longctx(args, world, rank, local):
                    "frac_hbm": round(achieved / hbm, 4)},
         "clocks": clk, "device_status": status,
     }
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    return line
 
 
 def main():

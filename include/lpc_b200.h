@@ -215,16 +215,22 @@ LPC_API int lpc_decode_attention_ragged(const void* q, const void* key_cache,
  * can synchronise the device or fail under memory pressure.
  * Same arguments and results as lpc_decode_attention, minus the workspace:
  * the split partials go to a fixed scratch array of LPC_NOALLOC_SCRATCH_BYTES
- * inside this library, held by every GPU that loads the library until the
- * process exits.  Shapes whose partials need more
- * (batch * heads * ceil(max_seq_len / 256) * (head_dim + 2) * 4 bytes) are
+ * inside this library.  The array belongs to the decode-attention module, so
+ * every GPU on which any decode-attention entry point (workspace, ragged or
+ * this one) has run holds those 24 MiB until the process exits.  Shapes whose
+ * partials need more
+ * (batch * heads * ceil(max_seq_len / 256) * (head_dim + 2) * 4 bytes), and
+ * sizes beyond the split grid (batch > 65535, max_seq_len > 65535 * 256), are
  * rejected with LPC_ERR_INVALID before anything runs.
- * The first call on a device looks up the array's device address (with that
- * device current); make that first call before any stream capture.
+ * The first call on a device, and the first call in a new CUDA context of a
+ * device (after a device reset), looks up the array's device address with
+ * that device current; make that first call before any stream capture.
  * All calls share the one array: calls that overlap on the GPU (two streams,
  * or two host threads) race on it; serialise them.  Nothing in it needs to
  * start at zero, each call writes every partial it reads.
  */
+/* Static device footprint of the library: 24 MiB per GPU once any decode
+ * attention has run on it (the scratch array of the entry point below). */
 #define LPC_NOALLOC_SCRATCH_BYTES (24u * 1024u * 1024u)
 LPC_API int lpc_decode_attention_noalloc(const void* q, const void* key_cache,
                                          const void* value_cache, const int32_t* seq_lens,

@@ -441,9 +441,19 @@ int launch_d(int G, const void* q, const void* kc, const void* vc, const int32_t
 
 }  // namespace
 
+// Largest sizes the split grid can express (grid.x = splits, grid.z = batch):
+// checked before any size arithmetic, so no product below can overflow.
+constexpr int64_t MAX_DECODE_BATCH = 65535;
+constexpr int64_t MAX_DECODE_SEQ = 65535LL * CHUNK;
+constexpr int MAX_DECODE_HEADS = 65535;
+constexpr int MAX_DECODE_HEAD_DIM = 1024;
+
 extern "C" int64_t lpc_decode_attention_workspace_bytes(int64_t batch, int heads,
                                                         int64_t max_seq_len, int head_dim) {
   if (batch <= 0 || heads <= 0 || max_seq_len <= 0 || head_dim <= 0) return 0;
+  if (batch > MAX_DECODE_BATCH || heads > MAX_DECODE_HEADS || max_seq_len > MAX_DECODE_SEQ ||
+      head_dim > MAX_DECODE_HEAD_DIM)
+    return 0;
   const int64_t max_splits = (max_seq_len + CHUNK - 1) / CHUNK;
   return batch * heads * max_splits * (int64_t)(head_dim + 2) * 4;
 }
@@ -471,6 +481,11 @@ int decode_common(const void* q, const void* key_cache, const void* value_cache,
   if (!aligned16(key_cache) || !aligned16(value_cache) || !aligned16(q) || !aligned16(out)) {
     set_error("decode_attention: tensors must be 16-byte aligned");
     return LPC_ERR_INVALID;
+  }
+  if (batch > MAX_DECODE_BATCH || heads > MAX_DECODE_HEADS || max_seq_len > MAX_DECODE_SEQ) {
+    set_error("decode_attention: grid too large (batch <= %lld, heads <= %d, max_seq_len <= %lld)",
+              (long long)MAX_DECODE_BATCH, MAX_DECODE_HEADS, (long long)MAX_DECODE_SEQ);
+    return LPC_ERR_UNSUPPORTED;
   }
   const int64_t need = lpc_decode_attention_workspace_bytes(batch, heads, max_seq_len, head_dim);
   if (!workspace || workspace_bytes < need || !aligned16(workspace)) {
@@ -553,7 +568,8 @@ extern "C" int lpc_decode_attention_ragged(const void* q, const void* key_cache,
 // cudaMalloc because an allocation may synchronise the device or fail under
 // memory pressure in the middle of a request.  For them the split partials
 // live in a fixed scratch array in this library's device memory instead of a
-// caller workspace.  Each GPU that loads the library holds this array
+// caller workspace.  The array belongs to this file's device code, so every
+// GPU on which any decode-attention kernel of the library has run holds it
 // (LPC_NOALLOC_SCRATCH_BYTES) until the process exits.
 // ---------------------------------------------------------------------------
 #include <mutex>
@@ -561,8 +577,16 @@ extern "C" int lpc_decode_attention_ragged(const void* q, const void* key_cache,
 static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[LPC_NOALLOC_SCRATCH_BYTES];
 
 namespace {
+// Device address of the scratch array, per device ordinal, together with the
+// CUDA context it was resolved in.  A device reset creates a new context in
+// which the module (and the array) may load at another address, so a cached
+// address is only reused while the context is the same one.
+struct NoallocSlot {
+  void* ctx;
+  void* addr;
+};
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[64] = {};  // device address of the scratch array, per device ordinal
+NoallocSlot g_noalloc[64] = {};
 }  // namespace
 
 extern "C" int lpc_decode_attention_noalloc(const void* q, const void* key_cache,
@@ -571,6 +595,17 @@ extern "C" int lpc_decode_attention_noalloc(const void* q, const void* key_cache
                                             int head_dim, int64_t max_batch, int64_t max_seq_len,
                                             float sm_scale, int dtype, void* stream) {
   using namespace lpc;
+  // sizes first: the scratch requirement below is only computed for sizes
+  // whose product cannot overflow
+  if (batch < 0 || batch > MAX_DECODE_BATCH || heads <= 0 || heads > MAX_DECODE_HEADS ||
+      max_seq_len <= 0 || max_seq_len > MAX_DECODE_SEQ || head_dim <= 0 ||
+      head_dim > MAX_DECODE_HEAD_DIM) {
+    set_error("decode_attention_noalloc: invalid sizes (batch=%lld heads=%d max_seq_len=%lld "
+              "head_dim=%d; batch <= %lld, heads <= %d, max_seq_len <= %lld)",
+              (long long)batch, heads, (long long)max_seq_len, head_dim,
+              (long long)MAX_DECODE_BATCH, MAX_DECODE_HEADS, (long long)MAX_DECODE_SEQ);
+    return LPC_ERR_INVALID;
+  }
   const int64_t need = lpc_decode_attention_workspace_bytes(batch, heads, max_seq_len, head_dim);
   if (need > (int64_t)LPC_NOALLOC_SCRATCH_BYTES) {
     set_error("decode_attention_noalloc: this shape needs %lld bytes of split scratch but the "
@@ -584,12 +619,15 @@ extern "C" int lpc_decode_attention_noalloc(const void* q, const void* key_cache
     set_error("decode_attention_noalloc: cannot query the current CUDA device");
     return LPC_ERR_CUDA;
   }
+  void* ctx = current_context();
   void* scratch = nullptr;
   {
-    // First call on a device: resolve the scratch array's device address with
-    // that device current (the symbol's host-side name is not a device pointer).
+    // First call on a device (or in a new context of it): resolve the scratch
+    // array's device address with that device current -- the symbol's
+    // host-side name is not a device pointer.
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_addr[dev]) {
+    NoallocSlot& slot = g_noalloc[dev];
+    if (!slot.addr || !ctx || slot.ctx != ctx) {
       void* p = nullptr;
       cudaError_t e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
       if (e != cudaSuccess || !p) {
@@ -597,9 +635,10 @@ extern "C" int lpc_decode_attention_noalloc(const void* q, const void* key_cache
                   cudaGetErrorString(e));
         return LPC_ERR_CUDA;
       }
-      g_noalloc_addr[dev] = p;
+      slot.addr = p;
+      slot.ctx = ctx;
     }
-    scratch = g_noalloc_addr[dev];
+    scratch = slot.addr;
   }
   // No clearing is needed: every partial the combine step reads is written by
   // the split step of the same call.

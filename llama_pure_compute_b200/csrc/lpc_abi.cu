@@ -71,6 +71,22 @@ int current_device_sms() {
   return v;
 }
 
+static PFN_cuCtxGetCurrent_v4000 g_ctx_get = nullptr;
+static std::once_flag g_ctx_once;
+
+void* current_context() {
+  std::call_once(g_ctx_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_get = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+  });
+  CUcontext c = nullptr;
+  if (!g_ctx_get || g_ctx_get(&c) != CUDA_SUCCESS) return nullptr;
+  return reinterpret_cast<void*>(c);
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 static std::once_flag g_encode_once;
 

@@ -46,6 +46,9 @@ bool aligned16(const void* p);
 // is per device context).  `mask` holds one bit per device ordinal.
 int once_per_device_smem(const void* kernel, int bytes, std::atomic<uint64_t>& mask);
 int current_device_sms();
+// The calling thread's current CUDA driver context (a CUcontext), or null when
+// the driver entry point is unavailable.
+void* current_context();
 
 // Encodes a 2-D row-major tensor map (inner dim contiguous) with 128-byte
 // swizzle.  Returns 0 on success.  `elem` is LPC_DTYPE_*.

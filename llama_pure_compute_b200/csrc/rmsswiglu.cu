@@ -420,38 +420,111 @@ __global__ void __launch_bounds__(192)
 
 // ---------------------------------------------------------------------------
 // fp32 streaming path
+//
+// The fp32 op is a weight stream: 8 token rows against 2 x [I, K] fp32
+// weights read once (361 MB for the 7B layer), ~2 FMA per weight byte.
+// Work is dealt out so that every warp streams the same number of bytes:
+//   * CTA c (one per SM) owns a contiguous range of inter-column pairs;
+//   * a unit is one pair (4 weight rows: gate/up of columns i and i+1) times
+//     one eighth of K; the CTA's units are dealt round-robin to its 16 warps
+//     (38 pairs x 8 = 304 units = 19 per warp for the 7B layer);
+//   * per unit a lane streams 4 float4 of each of the 4 rows, multiplies them
+//     by the 8 normalised token rows held in shared memory (each x float4 read
+//     serves 4 rows) and the warp reduces its 32 partial sums (4 rows x 8
+//     tokens) with a transposing butterfly (31 shuffles: lane j ends with sum
+//     j), written to a shared partial table;
+//   * once all units of a round are done, the 8 K-parts of each output are
+//     summed in fixed order, SiLU(g) * u, one write per output.
+// The RMSNorm prologue of the CTA's token rows runs while the first units'
+// weights are prefetched into L2.
 // ---------------------------------------------------------------------------
-constexpr int F32_ROWS = 8;
+constexpr int F32_ROWS = 8;        // token rows per CTA (blockIdx.y)
 constexpr int F32_WARPS = 16;
+constexpr int F32_KPARTS = 8;      // K is split in 8 parts per unit
+constexpr int F32_ROUND_PAIRS = 40;  // column pairs per round (partial table size)
+constexpr int F32_PART_FLOATS = F32_ROUND_PAIRS * F32_KPARTS * 32;
+
+// Transposing butterfly: v[0..31] of each lane summed over the warp; lane j
+// returns the total of value j.
+__device__ __forceinline__ float warp_transpose_sum32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const bool hi = (lane & o) != 0;
+#pragma unroll
+    for (int k = 0; k < o; ++k) {
+      const float send = hi ? v[k] : v[k + o];
+      const float keep = hi ? v[k + o] : v[k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return v[0];
+}
 
 template <typename W>
 __global__ void __launch_bounds__(F32_WARPS * 32, 1)
     swiglu_f32_kernel(const float* __restrict__ x, const W* __restrict__ nw,
                       const float* __restrict__ wg, const float* __restrict__ wu,
                       float* __restrict__ out, int64_t M, int K, int I, float eps) {
-  extern __shared__ float4 xs4[];  // [F32_ROWS][K/4]
+  extern __shared__ float4 xs4[];  // [F32_ROWS][K/4], then the partial table
+  __shared__ float red[F32_WARPS];
+  float* part = reinterpret_cast<float*>(xs4 + (int64_t)F32_ROWS * (K >> 2));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t m0 = (int64_t)blockIdx.y * F32_ROWS;
   const int rows = (int)min((int64_t)F32_ROWS, M - m0);
   const int kv = K >> 2;
+  const int pairs = (I + 1) >> 1;
+  const int p_begin = (int)((int64_t)blockIdx.x * pairs / gridDim.x);
+  const int p_end = (int)((int64_t)(blockIdx.x + 1) * pairs / gridDim.x);
 
-  // prologue: RMSNorm of this CTA's token rows into shared memory
-  for (int r = warp; r < F32_ROWS; r += F32_WARPS) {
+  // weight rows of unit u (pair p, K-part kp): gate/up of columns 2p, 2p+1
+  auto unit_rows = [&](int p, const float* (&r)[4]) {
+    const int i0 = 2 * p, i1 = min(2 * p + 1, I - 1);  // odd I: the last pair repeats a column
+    r[0] = wg + (int64_t)i0 * K;
+    r[1] = wu + (int64_t)i0 * K;
+    r[2] = wg + (int64_t)i1 * K;
+    r[3] = wu + (int64_t)i1 * K;
+  };
+
+  // L2 prefetch of each warp's first two units, under the norm prologue
+  for (int u = warp, n = 0; n < 2 && p_begin + u / F32_KPARTS < p_end; u += F32_WARPS, ++n) {
+    const float* r[4];
+    unit_rows(p_begin + u / F32_KPARTS, r);
+    const int kp = u % F32_KPARTS;
+    const int64_t k0 = (int64_t)kp * kv / F32_KPARTS * 4, k1 = (int64_t)(kp + 1) * kv / F32_KPARTS * 4;
+    for (int64_t k = k0 + lane * 32; k < k1; k += 32 * 32) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) asm volatile("prefetch.global.L2 [%0];" ::"l"(r[j] + k));
+    }
+  }
+
+  // prologue: RMSNorm of this CTA's token rows into shared memory; warp w
+  // takes half h = w & 1 of row w >> 1 (fp32 statistics, one rounding per
+  // product as in the reference's fp32 path)
+  {
+    const int r = warp >> 1, h = warp & 1;
+    const int v0 = h * (kv >> 1), v1 = h ? kv : (kv >> 1);
     float4* dst = xs4 + (int64_t)r * kv;
+    float ss = 0.f;
     if (r < rows) {
       const float4* src = reinterpret_cast<const float4*>(x + (m0 + r) * K);
-      float ss = 0.f;
-      for (int v = lane; v < kv; v += 32) {
+#pragma unroll 8
+      for (int v = v0 + lane; v < v1; v += 32) {
         const float4 a = __ldg(src + v);
         ss = fmaf(a.x, a.x, ss);
         ss = fmaf(a.y, a.y, ss);
         ss = fmaf(a.z, a.z, ss);
         ss = fmaf(a.w, a.w, ss);
       }
+    }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      const float rr = rsqrtf(ss / (float)K + eps);
-      for (int v = lane; v < kv; v += 32) {
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    const float rr = rsqrtf((red[2 * r] + red[2 * r + 1]) / (float)K + eps);
+    if (r < rows) {
+      const float4* src = reinterpret_cast<const float4*>(x + (m0 + r) * K);
+#pragma unroll 8
+      for (int v = v0 + lane; v < v1; v += 32) {
         const float4 a = __ldg(src + v);
         float4 o;
         o.x = __fmul_rn(__fmul_rn(a.x, rr), Num<W>::to_f(nw[4 * v + 0]));
@@ -461,79 +534,98 @@ __global__ void __launch_bounds__(F32_WARPS * 32, 1)
         dst[v] = o;
       }
     } else {
-      for (int v = lane; v < kv; v += 32) dst[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int v = v0 + lane; v < v1; v += 32) dst[v] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
   __syncthreads();
 
-  const int gw = blockIdx.x * F32_WARPS + warp;
-  const int nwarps = gridDim.x * F32_WARPS;
-  // rows gw, gw + nwarps, gw + 2*nwarps, ... taken two at a time
-  for (int i = gw; i < I; i += 2 * nwarps) {
-    const int i1 = i + nwarps;
-    const bool two = i1 < I;
-    const float4* g0p = reinterpret_cast<const float4*>(wg + (int64_t)i * K);
-    const float4* u0p = reinterpret_cast<const float4*>(wu + (int64_t)i * K);
-    const float4* g1p = two ? reinterpret_cast<const float4*>(wg + (int64_t)i1 * K) : g0p;
-    const float4* u1p = two ? reinterpret_cast<const float4*>(wu + (int64_t)i1 * K) : u0p;
-    float ag0[F32_ROWS], au0[F32_ROWS], ag1[F32_ROWS], au1[F32_ROWS];
+  for (int rp0 = p_begin; rp0 < p_end; rp0 += F32_ROUND_PAIRS) {
+    const int np = min(F32_ROUND_PAIRS, p_end - rp0);
+    for (int u = warp; u < np * F32_KPARTS; u += F32_WARPS) {
+      const int pl = u / F32_KPARTS, kp = u % F32_KPARTS;
+      const float* r[4];
+      unit_rows(rp0 + pl, r);
+      const int va = (int)((int64_t)kp * kv / F32_KPARTS), vb = (int)((int64_t)(kp + 1) * kv / F32_KPARTS);
+      {
+        // L2 prefetch of this warp's unit after the next (the first two were
+        // prefetched under the prologue): keeps DRAM requests in flight while
+        // the loads of this unit wait on L2 hits
+        const int un = u + 2 * F32_WARPS;
+        if (rp0 + un / F32_KPARTS < p_end) {
+          const float* rn[4];
+          unit_rows(rp0 + un / F32_KPARTS, rn);
+          const int kq = un % F32_KPARTS;
+          const int64_t k0 = (int64_t)kq * kv / F32_KPARTS * 4, k1 = (int64_t)(kq + 1) * kv / F32_KPARTS * 4;
+          for (int64_t k = k0 + lane * 32; k < k1; k += 32 * 32) {
 #pragma unroll
-    for (int r = 0; r < F32_ROWS; ++r) ag0[r] = au0[r] = ag1[r] = au1[r] = 0.f;
-#pragma unroll 4
-    for (int v = lane; v < kv; v += 32) {
-      const float4 g0 = __ldg(g0p + v), u0 = __ldg(u0p + v);
-      const float4 g1 = __ldg(g1p + v), u1 = __ldg(u1p + v);
-#pragma unroll
-      for (int r = 0; r < F32_ROWS; ++r) {
-        const float4 a = xs4[(int64_t)r * kv + v];
-        ag0[r] = fmaf(g0.x, a.x, ag0[r]); ag0[r] = fmaf(g0.y, a.y, ag0[r]);
-        ag0[r] = fmaf(g0.z, a.z, ag0[r]); ag0[r] = fmaf(g0.w, a.w, ag0[r]);
-        au0[r] = fmaf(u0.x, a.x, au0[r]); au0[r] = fmaf(u0.y, a.y, au0[r]);
-        au0[r] = fmaf(u0.z, a.z, au0[r]); au0[r] = fmaf(u0.w, a.w, au0[r]);
-        ag1[r] = fmaf(g1.x, a.x, ag1[r]); ag1[r] = fmaf(g1.y, a.y, ag1[r]);
-        ag1[r] = fmaf(g1.z, a.z, ag1[r]); ag1[r] = fmaf(g1.w, a.w, ag1[r]);
-        au1[r] = fmaf(u1.x, a.x, au1[r]); au1[r] = fmaf(u1.y, a.y, au1[r]);
-        au1[r] = fmaf(u1.z, a.z, au1[r]); au1[r] = fmaf(u1.w, a.w, au1[r]);
+            for (int j = 0; j < 4; ++j) asm volatile("prefetch.global.L2 [%0];" ::"l"(rn[j] + k));
+          }
+        }
       }
-    }
+      float acc[32];  // [row j][token t] at 8 * j + t
 #pragma unroll
-    for (int r = 0; r < F32_ROWS; ++r) {
+      for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+#pragma unroll 2
+      for (int v = va + lane; v < vb; v += 32) {
+        float4 w[4];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        ag0[r] += __shfl_xor_sync(0xffffffffu, ag0[r], o);
-        au0[r] += __shfl_xor_sync(0xffffffffu, au0[r], o);
-        ag1[r] += __shfl_xor_sync(0xffffffffu, ag1[r], o);
-        au1[r] += __shfl_xor_sync(0xffffffffu, au1[r], o);
+        for (int j = 0; j < 4; ++j) w[j] = __ldg(reinterpret_cast<const float4*>(r[j]) + v);
+#pragma unroll
+        for (int t = 0; t < F32_ROWS; ++t) {
+          const float4 a = xs4[(int64_t)t * kv + v];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float s = acc[8 * j + t];
+            s = fmaf(w[j].x, a.x, s);
+            s = fmaf(w[j].y, a.y, s);
+            s = fmaf(w[j].z, a.z, s);
+            s = fmaf(w[j].w, a.w, s);
+            acc[8 * j + t] = s;
+          }
+        }
       }
+      const float tot = warp_transpose_sum32(acc, lane);
+      part[(pl * F32_KPARTS + kp) * 32 + lane] = tot;
     }
-    if (lane < rows) {
-      // select this lane's row without dynamic register indexing
-      float g0 = 0.f, u0 = 0.f, g1 = 0.f, u1 = 0.f;
+    __syncthreads();
+    // outputs of the round: (token t, column c) with c fastest
+    const int ncols = min(2 * np, I - 2 * rp0);
+    for (int o = threadIdx.x; o < rows * ncols; o += blockDim.x) {
+      const int t = o / ncols, c = o - t * ncols;
+      const int pl = c >> 1, side = c & 1;  // row j: 2*side (gate), 2*side+1 (up)
+      const float* pp = part + pl * F32_KPARTS * 32;
+      float g = 0.f, uu = 0.f;
 #pragma unroll
-      for (int r = 0; r < F32_ROWS; ++r)
-        if (r == lane) { g0 = ag0[r]; u0 = au0[r]; g1 = ag1[r]; u1 = au1[r]; }
-      float* orow = out + (m0 + lane) * I;
-      orow[i] = (g0 / (1.0f + expf(-g0))) * u0;
-      if (two) orow[i1] = (g1 / (1.0f + expf(-g1))) * u1;
+      for (int kp = 0; kp < F32_KPARTS; ++kp) {
+        g += pp[kp * 32 + 8 * (2 * side) + t];
+        uu += pp[kp * 32 + 8 * (2 * side + 1) + t];
+      }
+      out[(m0 + t) * I + 2 * rp0 + c] = (g / (1.0f + expf(-g))) * uu;
     }
+    __syncthreads();
   }
 }
 
 template <typename W>
 int launch_f32(const void* x, const void* nw, const void* gw, const void* uw, void* out,
                int64_t M, int K, int I, float eps, cudaStream_t s) {
-  const size_t smem = (size_t)F32_ROWS * K * sizeof(float);
-  if (smem > 200 * 1024) {
+  const size_t smem = (size_t)F32_ROWS * K * sizeof(float) + (size_t)F32_PART_FLOATS * sizeof(float);
+  if (smem > 220 * 1024) {
     lpc::set_error("rmsswiglu_forward (fp32): dim %d too large for the fp32 path", K);
+    return LPC_ERR_UNSUPPORTED;
+  }
+  if (M > 65535LL * F32_ROWS) {
+    lpc::set_error("rmsswiglu_forward (fp32): at most %lld tokens", 65535LL * F32_ROWS);
     return LPC_ERR_UNSUPPORTED;
   }
   auto kfn = swiglu_f32_kernel<W>;
   static std::atomic<uint64_t> f32_mask{0};
-  int rcx = lpc::once_per_device_smem((const void*)kfn, 200 * 1024, f32_mask);
+  int rcx = lpc::once_per_device_smem((const void*)kfn, 220 * 1024, f32_mask);
   if (rcx) return rcx;
   const float* g = (const float*)gw;
   const float* u = uw ? (const float*)uw : g + (int64_t)I * K;
-  const int gx = std::max(1, std::min(lpc::current_device_sms(), (I + F32_WARPS - 1) / F32_WARPS));
+  const int pairs = (I + 1) / 2;
+  const int gx = std::max(1, std::min(lpc::current_device_sms(), pairs));
   const int64_t gy = (M + F32_ROWS - 1) / F32_ROWS;
   dim3 grid((unsigned)gx, (unsigned)gy);
   kfn<<<grid, F32_WARPS * 32, smem, s>>>((const float*)x, (const W*)nw, g, u, (float*)out, M, K, I,

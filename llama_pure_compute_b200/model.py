@@ -64,6 +64,18 @@ def precompute_freqs_cis(dim: int, end: int, theta: float = 10000.0,
     return torch.cos(f), torch.sin(f)
 
 
+def _weight_key(w: torch.Tensor):
+    """Identity of a weight's current contents for derived copies (stacked or
+    packed weights): storage, version counter, dtype, device.  Inference
+    tensors (a model built under torch.inference_mode) have no version
+    counter; they are keyed on their storage alone."""
+    try:
+        ver = w._version
+    except RuntimeError:
+        ver = None
+    return (w.data_ptr(), ver, w.dtype, w.device)
+
+
 class _StepContext:
     """Per-forward data shared by all layers (computed once, not per layer)."""
 
@@ -104,7 +116,7 @@ class LlamaAttention(nn.Module):
     def qkv_weight(self) -> torch.Tensor:
         """[(H+2Hkv)*D, dim] weight; q/k/v parameters are re-pointed into it once."""
         ws = (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
-        key = tuple((w.data_ptr(), w._version, w.dtype, w.device) for w in ws)
+        key = tuple(_weight_key(w) for w in ws)
         if self._qkv is None or key != self._qkv_key:
             fused = torch.cat([w.detach() for w in ws], dim=0).contiguous()
             n_q = self.num_heads * self.head_dim
@@ -115,7 +127,7 @@ class LlamaAttention(nn.Module):
                 self.v_proj.weight.data = fused[n_q + n_kv:]
             self._qkv = fused
             ws = (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
-            self._qkv_key = tuple((w.data_ptr(), w._version, w.dtype, w.device) for w in ws)
+            self._qkv_key = tuple(_weight_key(w) for w in ws)
         return self._qkv
 
     def packed_qkv(self):
@@ -204,7 +216,7 @@ class LlamaDecodeLayer(nn.Module):
         built on first use and rebuilt when either weight changes."""
         from .packed_linear import PackedWeight
         ws = (self.gate_proj.weight, self.up_proj.weight)
-        key = tuple((w.data_ptr(), w._version, w.dtype, w.device) for w in ws)
+        key = tuple(_weight_key(w) for w in ws)
         if self._packed_gate_up is None or key != self._packed_key:
             self._packed_gate_up = PackedWeight(ws[0], ws[1], layout="swiglu")
             self._packed_key = key

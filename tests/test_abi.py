@@ -87,6 +87,26 @@ def test_workspace_queries():
     assert n == 64 * 32 * 17 * 130 * 4
 
 
+def test_decode_sizes_that_would_overflow_are_rejected_on_the_host():
+    """Sizes beyond the split grid (65535 splits of 256 keys, 65535 sequences)
+    are refused before any size arithmetic: no wrapped, negative workspace
+    size can slip past a scratch or workspace check."""
+    lib = _lib.load()
+    big = 2**63 - 1
+    assert lib.lpc_decode_attention_workspace_bytes(1, 32, big, 128) == 0
+    assert lib.lpc_decode_attention_workspace_bytes(big, 32, 4096, 128) == 0
+    assert lib.lpc_decode_attention_workspace_bytes(1, 32, 65535 * 256 + 1, 128) == 0
+    assert lib.lpc_decode_attention_workspace_bytes(1, 1, 65535 * 256, 128) > 0
+    for b, s in ((1, big), (big, 4096), (65536, 4096), (1, 65535 * 256 + 1)):
+        rc = lib.lpc_decode_attention_noalloc(None, None, None, None, None, b, 32, 32, 128, b, s,
+                                              1.0, 2, None)
+        assert rc == _lib.LPC_ERR_INVALID, (b, s)
+        assert b"invalid sizes" in lib.lpc_last_error()
+    rc = lib.lpc_decode_attention(None, None, None, None, None, None, 0, 1, 32, 32, 128, 1, big,
+                                  1.0, 2, None)
+    assert rc != _lib.LPC_OK
+
+
 def test_error_translation():
     lib = _lib.load()
     lib.lpc_rmsnorm_forward(None, None, None, -1, 16, 1e-5, 2, 2, None)

@@ -461,6 +461,19 @@ def test_decode_op_shape_ragged():
     cos, sin = cos.to(torch.bfloat16).to(DEV), sin.to(torch.bfloat16).to(DEV)
     pos = L.view(B, 1).to(DEV)
     q = ops.rope_kv_append(qkv, pos, cos, sin, kc, vc, H, H)
+    # RoPE + append at this shape, bit-exact against the oracle: the rotated q
+    # and the appended K/V row of every sequence (the oracle writes sequence
+    # b's row into a small [B, H, B, D] cache at position b, rotating with the
+    # table row of position L_b)
+    qkv_c = qkv.cpu()
+    kr = torch.zeros(B, H, B, D, dtype=torch.bfloat16)
+    vr = torch.zeros_like(kr)
+    q_ref = rope_kv_append_ref(qkv_c, torch.arange(B).view(B, 1), cos.cpu()[L], sin.cpu()[L],
+                               kr, vr, H, H)
+    assert torch.equal(q.cpu(), q_ref)
+    idx = torch.arange(B)
+    assert torch.equal(kc[idx.to(DEV), :, L.to(DEV)].cpu(), kr[idx, :, idx])
+    assert torch.equal(vc[idx.to(DEV), :, L.to(DEV)].cpu(), vr[idx, :, idx])
     lens = (L + 1).to(torch.int32).to(DEV)
     o = ops.decode_attention(q.view(B, H, D), kc, vc, lens).float()
     worst = 0.0
