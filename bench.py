@@ -65,10 +65,12 @@ def parse():
                     help="untimed decode steps before the timed ones (default: enough to centre "
                          "the timed steps on the mean context)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--suite", choices=["decode", "ops", "longctx"], default="decode",
+    ap.add_argument("--suite", choices=["decode", "ops", "longctx", "kernels"], default="decode",
                     help="decode: the 7B decode workload (default); ops: per-op roofline lines; "
-                         "longctx: 64 prompts of 1k-8k tokens, prefill + 256 decode steps")
-    ap.add_argument("--only", default="", help="comma list of op lines for --suite ops")
+                         "longctx: 64 prompts of 1k-8k tokens, prefill + 256 decode steps; "
+                         "kernels: the per-kernel roofline entries of the decode line")
+    ap.add_argument("--only", default="", help="comma list of op lines for --suite ops, or of "
+                    "kernel keys for --suite kernels (" + ", ".join(KERNEL_KEYS) + ")")
     ap.add_argument("--no-kernels", action="store_true",
                     help="skip the per-kernel roofline block of the decode line")
     ap.add_argument("--no-longctx", action="store_true",
@@ -523,13 +525,18 @@ def _kentry(kernel, shape, us, *, nbytes=None, flops=None, hbm, tc, timing):
     return d
 
 
-def measure_kernels(dev):
+KERNEL_KEYS = ("swiglu_pair", "wsgemm_swiglu", "wsgemm_qkv", "prefill", "swiglu_f32",
+               "rope_kv_append", "kv_append", "rmsnorm", "decode")
+
+
+def measure_kernels(dev, only=None):
     """Device time of each hot-path kernel at its benchmark shape, with the
     algorithmic bytes / FLOPs of one launch and the fraction of the measured
     peaks (HBM copy GB/s; dense bf16 TF/s, burst).  Weight-streaming kernels are
     timed in steady state, launches back to back over distinct weights whose
     total exceeds L2 (what a decode step does); the others over inputs larger
-    than L2, or rotated over several input sets whose total exceeds it."""
+    than L2, or rotated over several input sets whose total exceeds it.
+    ``only``: a set of KERNEL_KEYS to measure (all by default)."""
     from llama_pure_compute_b200 import ops
     from llama_pure_compute_b200.flash_attention import flash_attention_v2
     from llama_pure_compute_b200.model import precompute_freqs_cis
@@ -547,103 +554,124 @@ def measure_kernels(dev):
     def rn(*shape, std=1.0, dtype=bf):
         return (std * torch.randn(*shape, device=dev, generator=g)).to(dtype)
 
+    want = lambda key: not only or key in only  # noqa: E731
+    w1 = torch.ones(D, device=dev, dtype=bf)
+    M = 32
+    B, S = 4, 2048
     with torch.inference_mode():
-        # SwiGLU of the 7B layer at 256 tokens: row norm + CTA-pair tcgen05 GEMM
-        M = 256
-        x = rn(M, D)
-        w1 = torch.ones(D, device=dev, dtype=bf)
-        ws = [rn(2 * I, D, std=0.02) for _ in range(6)]
-        empty = torch.empty(0, device=dev, dtype=bf)
-        us = _time_rotating([lambda w=w: ops.rmsswiglu_forward(x, w1, w, empty, 1e-5) for w in ws])
-        out.append(_kentry("rmsnorm_vec_kernel + swiglu_pair_kernel", "7B gate/up, 256 tokens", us,
-                           nbytes=2 * I * D * 2 + M * D * 2 + M * I * 2, flops=2 * M * D * 2 * I,
-                           hbm=hbm, tc=tc, timing=steady))
-        # decode-sized SwiGLU on packed weights (32 tokens)
-        pws = [PackedWeight(w, layout="swiglu") for w in ws]
-        M = 32
-        x = rn(M, D)
-        us = _time_rotating([lambda pw=pw: packed_linear(x, pw, "swiglu") for pw in pws])
-        out.append(_kentry("wsgemm_kernel (SwiGLU epilogue)", "7B gate/up, 32 tokens", us,
-                           nbytes=2 * I * D * 2 + M * D * 2 + M * I * 2, hbm=hbm, tc=tc,
-                           timing=steady))
-        del ws, pws
-        # q/k/v projection + RoPE + KV append (32 tokens)
-        wq = [rn(3 * H * 128, D, std=0.02) for _ in range(6)]
-        pq = [PackedWeight(w, layout="heads") for w in wq]
-        cos, sin = precompute_freqs_cis(128, 1024, device=dev)
-        cos, sin = cos.to(bf), sin.to(bf)
-        x = rn(M, 1, D)
-        pos = torch.randint(0, 1000, (M, 1), device=dev, generator=g)
-        kc = torch.zeros(M, H, 1024, 128, device=dev, dtype=bf)
-        vc = torch.zeros_like(kc)
-        us = _time_rotating([lambda pw=pw: ops.qkv_rope_append(x, pw, pos, cos, sin, kc, vc, H, H)
-                             for pw in pq])
-        out.append(_kentry("wsgemm_kernel (EPI_QKV: projection + RoPE + KV append)",
-                           "7B q/k/v, 32 tokens", us,
-                           nbytes=3 * H * 128 * D * 2 + M * D * 2 + M * 3 * H * 128 * 2, hbm=hbm,
-                           tc=tc, timing=steady))
-        del wq, pq, kc, vc
-        # prefill attention [4, 32, 2048, 128] causal
-        q, k, v = (rn(4, 32, 2048, 128) for _ in range(3))
-        us = _time_us(lambda: flash_attention_v2(q, k, v, causal=True, sm_scale=128 ** -0.5), 10)
-        out.append(_kentry("flash_prefill_kernel", "[4, 32, 2048, 128] causal", us,
-                           nbytes=4 * 4 * 32 * 2048 * 128 * 2,
-                           flops=2 * 4 * 32 * 2048 * 2048 * 128, hbm=hbm, tc=tc,
-                           timing="inputs 201 MB (> L2), launches back to back"))
-        del q, k, v
-        # fp32 RMSNorm + SwiGLU op shape (x [8, 4096], W 2 x [11008, 4096] fp32)
-        xf = rn(8, D, dtype=torch.float32)
-        wf = 1 + 0.02 * torch.randn(D, device=dev, generator=g)
-        gu = [(rn(I, D, std=0.02, dtype=torch.float32), rn(I, D, std=0.02, dtype=torch.float32))
-              for _ in range(2)]
-        us = _time_rotating([lambda a=a, b=b: ops.rmsswiglu_forward(xf, wf, a, b, 1e-6)
-                             for a, b in gu])
-        out.append(_kentry("swiglu_f32_kernel", "fp32 op: x [8, 4096], W 2 x [11008, 4096]", us,
-                           nbytes=(2 * I * D + 8 * D + D + 8 * I) * 4, hbm=hbm, tc=tc,
-                           timing=steady))
-        del gu
-        # RoPE + KV append at a prefill size: 4 x 2048 tokens
-        B, S = 4, 2048
-        sets = []
-        cos, sin = precompute_freqs_cis(128, S, device=dev)
-        cos, sin = cos.to(bf), sin.to(bf)
-        posp = torch.arange(S, device=dev).unsqueeze(0).expand(B, -1).contiguous()
-        for _ in range(3):
-            sets.append((rn(B, S, 3 * H * 128), torch.empty(B, H, S, 128, device=dev, dtype=bf),
-                         torch.empty(B, H, S, 128, device=dev, dtype=bf),
-                         torch.empty(B, H, S, 128, device=dev, dtype=bf),
-                         rn(B * S, H, 128), rn(B * S, H, 128)))
-        us = _time_rotating([lambda t=t: ops.rope_kv_append(t[0], posp, cos, sin, t[1], t[2], H, H,
-                                                            q_out=t[3]) for t in sets])
-        out.append(_kentry("rope_kv_append_kernel", "4 x 2048 tokens, 32 + 2 x 32 heads", us,
-                           nbytes=2 * B * S * 3 * H * 128 * 2, hbm=hbm, tc=tc, timing=rot))
-        # KV append alone (update_kv_cache) at the same size
-        us = _time_rotating([lambda t=t: ops.update_kv_cache(t[4], t[5], t[1], t[2]) for t in sets])
-        out.append(_kentry("kv_append_kernel", "8192 tokens x 32 heads x 128 (K and V)", us,
-                           nbytes=2 * 2 * B * S * H * 128 * 2, hbm=hbm, tc=tc, timing=rot))
-        del sets
-        # row RMSNorm at 8192 x 4096
-        xs = [rn(B * S, D) for _ in range(4)]
-        us = _time_rotating([lambda t=t: ops.rmsnorm_forward(t, w1, 1e-5) for t in xs])
-        out.append(_kentry("rmsnorm_vec_kernel", "8192 x 4096", us,
-                           nbytes=2 * B * S * D * 2 + D * 2, hbm=hbm, tc=tc, timing=rot))
-        del xs
-        # decode attention at the decode op shape: 64 sequences, L ~ U[128, 4096]
-        torch.manual_seed(2)
-        L = torch.randint(128, 4097, (64,))
-        Smax = 4097
-        kc = rn(64, H, Smax, 128)
-        vc = rn(64, H, Smax, 128)
-        qd = rn(64, H, 128)
-        lens = (L + 1).to(torch.int32).to(dev)
-        wsd = ops.decode_attention_workspace(64, H, Smax, 128, dev)
-        od = torch.empty_like(qd)
-        us = _time_us(lambda: ops.decode_attention(qd, kc, vc, lens, None, od, wsd), 10)
-        out.append(_kentry("decode_split_kernel + decode_combine_kernel",
-                           "64 sequences, L ~ U[128, 4096], 32 heads x 128", us,
-                           nbytes=int((L + 1).sum()) * H * 128 * 2 * 2 + 2 * 64 * H * 128 * 2,
-                           hbm=hbm, tc=tc, timing="4.3 GB cache (> L2), launches back to back"))
-        del kc, vc
+        if want("swiglu_pair") or want("wsgemm_swiglu"):
+            ws = [rn(2 * I, D, std=0.02) for _ in range(6)]
+        if want("swiglu_pair"):
+            # SwiGLU of the 7B layer at 256 tokens: the norm inside the
+            # CTA-pair tcgen05 GEMM (norm weight folded into gate/up)
+            M = 256
+            x = rn(M, D)
+            us = _time_rotating([lambda w=w: ops.rmsswiglu_folded_forward(x, w, None, 1e-5)
+                                 for w in ws])
+            out.append(_kentry("swiglu_pair_kernel (norm inside)", "7B gate/up, 256 tokens", us,
+                               nbytes=2 * I * D * 2 + M * D * 2 + M * I * 2,
+                               flops=2 * M * D * 2 * I, hbm=hbm, tc=tc, timing=steady))
+        if want("wsgemm_swiglu"):
+            # decode-sized norm + SwiGLU on packed weights (32 tokens)
+            pws = [PackedWeight(w, layout="swiglu", norm_weight=w1) for w in ws]
+            M = 32
+            x = rn(M, D)
+            us = _time_rotating([lambda pw=pw: packed_linear(x, pw, "swiglu", norm_eps=1e-5)
+                                 for pw in pws])
+            out.append(_kentry("wsgemm_kernel (norm + SwiGLU epilogue)", "7B gate/up, 32 tokens",
+                               us, nbytes=2 * I * D * 2 + M * D * 2 + M * I * 2, hbm=hbm, tc=tc,
+                               timing=steady))
+            del pws
+        if want("swiglu_pair") or want("wsgemm_swiglu"):
+            del ws
+        if want("wsgemm_qkv"):
+            # input norm + q/k/v projection + RoPE + KV append (32 tokens)
+            M = 32
+            wq = [rn(3 * H * 128, D, std=0.02) for _ in range(6)]
+            pq = [PackedWeight(w, layout="heads", norm_weight=w1) for w in wq]
+            cos, sin = precompute_freqs_cis(128, 1024, device=dev)
+            cos, sin = cos.to(bf), sin.to(bf)
+            x = rn(M, 1, D)
+            pos = torch.randint(0, 1000, (M, 1), device=dev, generator=g)
+            kc = torch.zeros(M, H, 1024, 128, device=dev, dtype=bf)
+            vc = torch.zeros_like(kc)
+            us = _time_rotating([lambda pw=pw: ops.qkv_rope_append(x, pw, pos, cos, sin, kc, vc, H,
+                                                                   H, norm_eps=1e-5) for pw in pq])
+            out.append(_kentry("wsgemm_kernel (EPI_QKV: norm + projection + RoPE + KV append)",
+                               "7B q/k/v, 32 tokens", us,
+                               nbytes=3 * H * 128 * D * 2 + M * D * 2 + M * 3 * H * 128 * 2,
+                               hbm=hbm, tc=tc, timing=steady))
+            del wq, pq, kc, vc
+        if want("prefill"):
+            # prefill attention [4, 32, 2048, 128] causal
+            q, k, v = (rn(4, 32, 2048, 128) for _ in range(3))
+            us = _time_us(lambda: flash_attention_v2(q, k, v, causal=True, sm_scale=128 ** -0.5), 10)
+            out.append(_kentry("flash_prefill_kernel", "[4, 32, 2048, 128] causal", us,
+                               nbytes=4 * 4 * 32 * 2048 * 128 * 2,
+                               flops=2 * 4 * 32 * 2048 * 2048 * 128, hbm=hbm, tc=tc,
+                               timing="inputs 201 MB (> L2), launches back to back"))
+            del q, k, v
+        if want("swiglu_f32"):
+            # fp32 RMSNorm + SwiGLU op shape (x [8, 4096], W 2 x [11008, 4096] fp32)
+            xf = rn(8, D, dtype=torch.float32)
+            wf = 1 + 0.02 * torch.randn(D, device=dev, generator=g)
+            gu = [(rn(I, D, std=0.02, dtype=torch.float32), rn(I, D, std=0.02, dtype=torch.float32))
+                  for _ in range(2)]
+            us = _time_rotating([lambda a=a, b=b: ops.rmsswiglu_forward(xf, wf, a, b, 1e-6)
+                                 for a, b in gu])
+            out.append(_kentry("swiglu_f32_kernel", "fp32 op: x [8, 4096], W 2 x [11008, 4096]", us,
+                               nbytes=(2 * I * D + 8 * D + D + 8 * I) * 4, hbm=hbm, tc=tc,
+                               timing=steady))
+            del gu
+        if want("rope_kv_append") or want("kv_append"):
+            # RoPE + KV append at a prefill size: 4 x 2048 tokens
+            sets = []
+            cos, sin = precompute_freqs_cis(128, S, device=dev)
+            cos, sin = cos.to(bf), sin.to(bf)
+            posp = torch.arange(S, device=dev).unsqueeze(0).expand(B, -1).contiguous()
+            for _ in range(3):
+                sets.append((rn(B, S, 3 * H * 128), torch.empty(B, H, S, 128, device=dev, dtype=bf),
+                             torch.empty(B, H, S, 128, device=dev, dtype=bf),
+                             torch.empty(B, H, S, 128, device=dev, dtype=bf),
+                             rn(B * S, H, 128), rn(B * S, H, 128)))
+        if want("rope_kv_append"):
+            us = _time_rotating([lambda t=t: ops.rope_kv_append(t[0], posp, cos, sin, t[1], t[2], H,
+                                                                H, q_out=t[3]) for t in sets])
+            out.append(_kentry("rope_kv_append_kernel", "4 x 2048 tokens, 32 + 2 x 32 heads", us,
+                               nbytes=2 * B * S * 3 * H * 128 * 2, hbm=hbm, tc=tc, timing=rot))
+        if want("kv_append"):
+            # KV append alone (update_kv_cache) at the same size
+            us = _time_rotating([lambda t=t: ops.update_kv_cache(t[4], t[5], t[1], t[2])
+                                 for t in sets])
+            out.append(_kentry("kv_append_kernel", "8192 tokens x 32 heads x 128 (K and V)", us,
+                               nbytes=2 * 2 * B * S * H * 128 * 2, hbm=hbm, tc=tc, timing=rot))
+        if want("rope_kv_append") or want("kv_append"):
+            del sets
+        if want("rmsnorm"):
+            # row RMSNorm at 8192 x 4096
+            xs = [rn(B * S, D) for _ in range(4)]
+            us = _time_rotating([lambda t=t: ops.rmsnorm_forward(t, w1, 1e-5) for t in xs])
+            out.append(_kentry("rmsnorm_vec_kernel", "8192 x 4096", us,
+                               nbytes=2 * B * S * D * 2 + D * 2, hbm=hbm, tc=tc, timing=rot))
+            del xs
+    if want("decode"):
+        with torch.inference_mode():
+            # decode attention at the decode op shape: 64 sequences, L ~ U[128, 4096]
+            torch.manual_seed(2)
+            L = torch.randint(128, 4097, (64,))
+            Smax = 4097
+            kc = rn(64, H, Smax, 128)
+            vc = rn(64, H, Smax, 128)
+            qd = rn(64, H, 128)
+            lens = (L + 1).to(torch.int32).to(dev)
+            wsd = ops.decode_attention_workspace(64, H, Smax, 128, dev)
+            od = torch.empty_like(qd)
+            us = _time_us(lambda: ops.decode_attention(qd, kc, vc, lens, None, od, wsd), 10)
+            out.append(_kentry("decode_split_kernel + decode_combine_kernel",
+                               "64 sequences, L ~ U[128, 4096], 32 heads x 128", us,
+                               nbytes=int((L + 1).sum()) * H * 128 * 2 * 2 + 2 * 64 * H * 128 * 2,
+                               hbm=hbm, tc=tc, timing="4.3 GB cache (> L2), launches back to back"))
+            del kc, vc
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     return out
@@ -905,9 +933,23 @@ def longctx_measure(args, world, rank, local):
                           n_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim,
                           dtype=torch.bfloat16, device=dev)
     free, _ = torch.cuda.mem_get_info(dev)
-    # the packed SwiGLU copy costs 2 * 11008 * 4096 * 2 B per layer: keep it only with room to spare
-    packed = free > 12e9 and len(mine) <= 128
-    model.model.packed_swiglu_max_tokens = 128 if packed else 0
+    # packed weight copies for the decode-sized kernels, per layer: q/k/v
+    # 100.7 MB, gate/up 180.4 MB, o_proj 33.6 MB + down_proj 90.2 MB; each is
+    # kept only when this rank's step uses it and 2 GB stay free
+    from llama_pure_compute_b200 import model as model_mod
+    n, L, spare = len(mine), cfg.num_layers, free - 2e9
+    use = {}
+    for name, limit, nbytes in (("qkv", model_mod.FUSED_QKV_MAX_TOKENS, 100.7e6),
+                                ("swiglu", model_mod.PACKED_SWIGLU_MAX_TOKENS, 180.4e6),
+                                ("residual", model_mod.PACKED_RESIDUAL_MAX_TOKENS, 123.8e6)):
+        use[name] = n <= limit and spare > L * nbytes
+        if use[name]:
+            spare -= L * nbytes
+    mm = model.model
+    mm.fused_qkv_max_tokens = model_mod.FUSED_QKV_MAX_TOKENS if use["qkv"] else 0
+    mm.packed_swiglu_max_tokens = model_mod.PACKED_SWIGLU_MAX_TOKENS if use["swiglu"] else 0
+    mm.packed_residual_max_tokens = model_mod.PACKED_RESIDUAL_MAX_TOKENS if use["residual"] else 0
+    packed = use
     dec = BatchedGreedyDecoder(model, cache, len(mine), use_cuda_graph=True, prefill_chunk=1)
 
     barrier(world)
@@ -959,7 +1001,7 @@ def longctx_measure(args, world, rank, local):
                    "sum_prompt_tokens": sum_p, "prompt_len_min": min(lens),
                    "prompt_len_max": max(lens), "partition": "LPT on prompt+256",
                    "rank_loads": loads, "kv_cache_gb_rank0": kv_gb,
-                   "packed_swiglu": packed},
+                   "packed_copies": packed},
         "prefill": {"tokens": sum_p, "ms": round(prefill_ms, 1),
                     "tok_s": round(sum_p / (prefill_ms / 1e3), 1),
                     "tflops": round(prefill_flops / (prefill_ms / 1e3) / 1e12 / world, 1),
@@ -979,6 +1021,12 @@ def main():
     args = parse()
     if args.suite == "ops":
         run_ops(args)
+        return
+    if args.suite == "kernels":
+        torch.cuda.set_device(0)
+        only = set(filter(None, args.only.split(","))) or None
+        for e in measure_kernels(torch.device("cuda", 0), only):
+            print(json.dumps(e), flush=True)
         return
     if args.suite == "longctx":
         world, rank, local = dist_setup()

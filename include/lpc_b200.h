@@ -148,12 +148,29 @@ LPC_API int lpc_rmsswiglu_forward(const void* x, const void* rms_weight, const v
  * with row strides given in elements between consecutive positions
  * (k_seq_stride) and heads (k_head_stride), batches (k_batch_stride), so a
  * slice of a preallocated cache can be passed without a copy.
- * out: [batch, heads, q_len, head_dim].  head_dim 128, bf16 or fp16.
+ * out: [batch, heads, q_len, head_dim].  head_dim 64 or 128, bf16 or fp16 (the
+ * Python entry point runs head_dim 32 through the 64 kernel on zero-padded rows).
  */
 LPC_API int lpc_flash_attention(const void* q, const void* k, const void* v, void* out, int64_t batch,
                         int heads, int kv_heads, int64_t q_len, int64_t kv_len, int head_dim,
                         int64_t k_batch_stride, int64_t k_head_stride, int causal, float sm_scale,
                         int dtype, void* stream);
+
+/*
+ * RMSNorm + SwiGLU in one kernel, for weights that already carry the norm
+ * weight: gate_w / up_w hold W[n, k] * rms_weight[k] (e.g. folded once when a
+ * model is loaded; up_w NULL: gate_w is the fused [2 * inter, dim] form).
+ *   out = silu(rsqrt(mean(x^2) + eps) * x gate_w^T) * (rsqrt(...) * x up_w^T)
+ * Replaces: rmsswiglu_forward's three steps (rmsswiglu.cu:176-196: norm into
+ *           an HBM buffer, GEMM, activation) for a caller that owns its weights.
+ * The CTA-pair tcgen05 GEMM takes each token row's sum of squares from the
+ * activation tiles it feeds the tensor core and scales the fp32 accumulators
+ * in the epilogue: no normalised copy of x is written.  bf16 or fp16, dim a
+ * multiple of 64, inter of 16.  No workspace.
+ */
+LPC_API int lpc_rmsswiglu_folded_forward(const void* x, const void* gate_w, const void* up_w,
+                                         void* out, int64_t tokens, int dim, int inter, float eps,
+                                         int dtype, void* stream);
 
 /*
  * Split-KV decode attention over ragged per-sequence context lengths
@@ -163,7 +180,7 @@ LPC_API int lpc_flash_attention(const void* q, const void* k, const void* v, voi
  *           array of lengths.
  * q: [batch, heads, head_dim]; caches [max_batch, kv_heads, max_seq_len, head_dim];
  * seq_lens: int32 [batch] on the device, keys [0, seq_lens[b]) are attended;
- * out: [batch, heads, head_dim].
+ * out: [batch, heads, head_dim].  head_dim 32, 64 or 128; bf16 or fp16.
  * workspace: lpc_decode_attention_workspace_bytes(batch, heads, max_seq_len, head_dim)
  * bytes (per-split partial results).
  */
@@ -252,14 +269,18 @@ LPC_API int lpc_decode_attention_noalloc(const void* q, const void* key_cache,
  *           projection weights stacked, head_dim 128); each head's rows are
  *           interleaved so that the rotate-half partners d and d + 64 meet in
  *           one warp of the epilogue (lpc_qkv_rope_append).
+ * k_scale: NULL, or k fp32 factors that multiply column k of every weight row
+ * (W[n, k] * k_scale[k], one rounding): the weight of the RMSNorm whose output
+ * the projection consumes, folded in so that lpc_wsgemm / lpc_qkv_rope_append
+ * can normalise inside the GEMM (norm_eps > 0 there).
  * packed: lpc_packed_weight_bytes(n_out, k, layout) bytes, 16-byte aligned.
  * k must be a multiple of 64; bf16 or fp16.  Returns after the packed copy is
  * complete (the call synchronises `stream`): lpc_wsgemm starts reading the
  * weights before it waits on the previous kernel of its stream.
  */
 LPC_API int64_t lpc_packed_weight_bytes(int64_t n_out, int k, int layout);
-LPC_API int lpc_pack_weights(const void* w0, const void* w1, void* packed, int64_t n_out, int k,
-                             int layout, int dtype, void* stream);
+LPC_API int lpc_pack_weights(const void* w0, const void* w1, const float* k_scale, void* packed,
+                             int64_t n_out, int k, int layout, int dtype, void* stream);
 
 /*
  * Decode-sized GEMM against packed weights:
@@ -274,6 +295,12 @@ LPC_API int lpc_pack_weights(const void* w0, const void* w1, void* packed, int64
  * epilogue 2: out = silu(x Wg^T) * (x Wu^T)    (packed with layout 1; out [tokens, n_out])
  * x: [tokens, k] contiguous; fp32 accumulation, one rounding to the dtype.
  * n_out <= 2^24.  No workspace.
+ * norm_eps > 0 fuses the RMSNorm that feeds the projection (triton_kernels/
+ * rmsnorm.py:58-96): x are the raw rows, the norm weight is folded into the
+ * packed weight (lpc_pack_weights' k_scale), and every token's accumulators
+ * are scaled by rsqrt(mean(x^2) + norm_eps) -- the sums of squares are taken
+ * from the activation tiles the MMA reads, so no normalised copy of x is
+ * written.  norm_eps = 0: x is used as given.
  * Split k: when there are few weight tiles the launch runs clusters of up to
  * 8 CTAs per tile, each on a share of k, reduce-scattered through
  * distributed shared memory (deterministic: fixed rank order).  Launched with
@@ -282,7 +309,8 @@ LPC_API int lpc_pack_weights(const void* w0, const void* w1, void* packed, int64
  * is read before it completes.
  */
 LPC_API int lpc_wsgemm(const void* x, const void* packed_w, void* out, const void* resid,
-                       int64_t tokens, int64_t n_out, int k, int epilogue, int dtype, void* stream);
+                       int64_t tokens, int64_t n_out, int k, int epilogue, int dtype,
+                       float norm_eps, void* stream);
 
 /*
  * Fused projection + RoPE + KV append of the attention block for decode-sized
@@ -300,6 +328,8 @@ LPC_API int lpc_wsgemm(const void* x, const void* packed_w, void* out, const voi
  * 128]) and lpc_rope_kv_append_ragged ([Hkv, total_rows, 128] at
  * seq_base[b] + pos, pos < seq_cap[b]).  Out-of-range positions or rows set
  * LPC_DEV_ERR_BOUNDS and skip the token.  head_dim must be 128; bf16 or fp16.
+ * norm_eps > 0: x are the raw hidden states and the input RMSNorm runs inside
+ * the kernel, as for lpc_wsgemm (its weight folded into the packed weight).
  */
 LPC_API int lpc_qkv_rope_append(const void* x, const void* packed_w, const int64_t* positions,
                                 const void* cos, const void* sin, int64_t table_rows, void* q_out,
@@ -307,7 +337,7 @@ LPC_API int lpc_qkv_rope_append(const void* x, const void* packed_w, const int64
                                 const int32_t* seq_cap, int64_t batch, int64_t seq, int num_heads,
                                 int num_kv_heads, int head_dim, int k, int64_t max_batch,
                                 int64_t max_seq_len, int64_t total_rows, int dtype, int table_dtype,
-                                void* stream);
+                                float norm_eps, void* stream);
 
 #ifdef __cplusplus
 }

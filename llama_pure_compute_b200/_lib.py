@@ -44,6 +44,7 @@ SIGNATURES = {
     "lpc_rmsswiglu_forward": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _F, _I, _I, _P]),
     "lpc_flash_attention": (_I, [_P, _P, _P, _P, _I64, _I, _I, _I64, _I64, _I, _I64, _I64, _I, _F,
                                  _I, _P]),
+    "lpc_rmsswiglu_folded_forward": (_I, [_P, _P, _P, _P, _I64, _I, _I, _F, _I, _P]),
     "lpc_decode_attention_workspace_bytes": (_I64, [_I64, _I, _I64, _I]),
     "lpc_decode_attention": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _I64, _I64, _F,
                                   _I, _P]),
@@ -54,10 +55,10 @@ SIGNATURES = {
     "lpc_decode_attention_ragged": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I,
                                          _I64, _I64, _F, _I, _P]),
     "lpc_packed_weight_bytes": (_I64, [_I64, _I, _I]),
-    "lpc_pack_weights": (_I, [_P, _P, _P, _I64, _I, _I, _I, _P]),
-    "lpc_wsgemm": (_I, [_P, _P, _P, _P, _I64, _I64, _I, _I, _I, _P]),
+    "lpc_pack_weights": (_I, [_P, _P, _P, _P, _I64, _I, _I, _I, _P]),
+    "lpc_wsgemm": (_I, [_P, _P, _P, _P, _I64, _I64, _I, _I, _I, _F, _P]),
     "lpc_qkv_rope_append": (_I, [_P, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I, _I,
-                                 _I, _I, _I64, _I64, _I64, _I, _I, _P]),
+                                 _I, _I, _I64, _I64, _I64, _I, _I, _F, _P]),
 }
 
 _lib = None
@@ -69,7 +70,7 @@ KERNELS_PER_CALL = {
     "lpc_rmsnorm_forward": 1, "lpc_rmsswiglu_forward": 2, "lpc_flash_attention": 1,
     "lpc_decode_attention": 2, "lpc_decode_attention_noalloc": 2,
     "lpc_pack_weights": 1, "lpc_wsgemm": 1, "lpc_qkv_rope_append": 1, "lpc_rope_kv_append_ragged": 1,
-    "lpc_decode_attention_ragged": 2,
+    "lpc_decode_attention_ragged": 2, "lpc_rmsswiglu_folded_forward": 1,
 }
 launch_count = 0
 

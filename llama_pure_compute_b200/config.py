@@ -7,8 +7,7 @@ hot path reads is kept (no C++ header generator).
 from __future__ import annotations
 
 import json
-import os
-from dataclasses import asdict, dataclass, field
+from dataclasses import dataclass, field
 from enum import Enum
 from pathlib import Path
 from typing import Any, Dict, Optional, Union
@@ -92,22 +91,6 @@ class LlamaModelConfig:
             "num_key_value_heads": "num_kv_heads",
         }
         return cls.from_dict({mapping.get(k, k): v for k, v in data.items()})
-
-    @classmethod
-    def from_env(cls) -> "LlamaModelConfig":
-        env: Dict[str, Any] = {}
-        if "LLAMA_MAX_BATCH_SIZE" in os.environ:
-            env["max_batch_size"] = int(os.environ["LLAMA_MAX_BATCH_SIZE"])
-        if "LLAMA_MAX_SEQ_LEN" in os.environ:
-            env["max_seq_len"] = int(os.environ["LLAMA_MAX_SEQ_LEN"])
-        if "LLAMA_PRECISION" in os.environ:
-            env["precision"] = Precision(os.environ["LLAMA_PRECISION"].lower())
-        return cls.from_dict(env)
-
-    def to_json(self, output_path: Union[str, Path]) -> None:
-        data = asdict(self)
-        data["precision"] = self.precision.value
-        Path(output_path).write_text(json.dumps(data, indent=2), encoding="utf-8")
 
 
 PRESETS: Dict[str, LlamaModelConfig] = {

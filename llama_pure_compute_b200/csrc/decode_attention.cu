@@ -90,6 +90,54 @@ struct RawRow<2> {
   uint32_t w[1];
   __device__ __forceinline__ void load(const uint8_t* p) { w[0] = *reinterpret_cast<const uint32_t*>(p); }
 };
+template <>
+struct RawRow<1> {  // head_dim 32: one 16-bit value per lane
+  uint32_t w[1];
+  __device__ __forceinline__ void load(const uint8_t* p) { w[0] = *reinterpret_cast<const uint16_t*>(p); }
+};
+
+template <typename T>
+__device__ __forceinline__ float unpack1(uint32_t w);
+template <>
+__device__ __forceinline__ float unpack1<__nv_bfloat16>(uint32_t w) { return __uint_as_float(w << 16); }
+template <>
+__device__ __forceinline__ float unpack1<__half>(uint32_t w) {
+  return __half2float(__ushort_as_half((unsigned short)w));
+}
+
+// q . k over this lane's DPL dims (fixed order).
+template <typename T, int DPL>
+__device__ __forceinline__ float row_dot(const RawRow<DPL>& r, const float* qf) {
+  if constexpr (DPL == 1) {
+    return qf[0] * unpack1<T>(r.w[0]);
+  } else {
+    float acc_d = 0.f;
+#pragma unroll
+    for (int w = 0; w < DPL / 2; ++w) {
+      float a, c;
+      unpack2<T>(r.w[w], a, c);
+      acc_d = fmaf(qf[2 * w], a, acc_d);
+      acc_d = fmaf(qf[2 * w + 1], c, acc_d);
+    }
+    return acc_d;
+  }
+}
+
+// acc += p * v over this lane's DPL dims.
+template <typename T, int DPL>
+__device__ __forceinline__ void row_axpy(const RawRow<DPL>& r, float p, float* acc) {
+  if constexpr (DPL == 1) {
+    acc[0] = fmaf(p, unpack1<T>(r.w[0]), acc[0]);
+  } else {
+#pragma unroll
+    for (int w = 0; w < DPL / 2; ++w) {
+      float a, c;
+      unpack2<T>(r.w[w], a, c);
+      acc[2 * w] = fmaf(p, a, acc[2 * w]);
+      acc[2 * w + 1] = fmaf(p, c, acc[2 * w + 1]);
+    }
+  }
+}
 
 // Where a sequence's cache rows live.
 //   dense  (base == nullptr): cache [max_batch, Hkv, Smax, D], row (b, h, p) =
@@ -211,7 +259,7 @@ __global__ void __launch_bounds__((NCWARPS + 1) * 32)
           vr[j].load(vb + j * ROW_BYTES);
         } else {
 #pragma unroll
-          for (int w = 0; w < DPL / 2; ++w) { kr[j].w[w] = 0u; vr[j].w[w] = 0u; }
+          for (int w = 0; w < (DPL + 1) / 2; ++w) { kr[j].w[w] = 0u; vr[j].w[w] = 0u; }
         }
       }
       __syncwarp();
@@ -221,17 +269,7 @@ __global__ void __launch_bounds__((NCWARPS + 1) * 32)
       for (int g = 0; g < G; ++g) {
         float p8[KPW];
 #pragma unroll
-        for (int j = 0; j < KPW; ++j) {
-          float acc_d = 0.f;
-#pragma unroll
-          for (int w = 0; w < DPL / 2; ++w) {
-            float a, c;
-            unpack2<T>(kr[j].w[w], a, c);
-            acc_d = fmaf(qf[g][2 * w], a, acc_d);
-            acc_d = fmaf(qf[g][2 * w + 1], c, acc_d);
-          }
-          p8[j] = acc_d;
-        }
+        for (int j = 0; j < KPW; ++j) p8[j] = row_dot<T, DPL>(kr[j], qf[g]);
         // transposing butterfly: 8 keys x 32 lanes -> lanes 4j..4j+3 hold key j
         {
           const bool hi = lane & 16;
@@ -275,13 +313,7 @@ __global__ void __launch_bounds__((NCWARPS + 1) * 32)
 #pragma unroll
         for (int j = 0; j < KPW; ++j) {
           const float pj = __shfl_sync(0xffffffffu, p, 4 * j);
-#pragma unroll
-          for (int w = 0; w < DPL / 2; ++w) {
-            float a, c;
-            unpack2<T>(vr[j].w[w], a, c);
-            acc[g][2 * w] = fmaf(pj, a, acc[g][2 * w]);
-            acc[g][2 * w + 1] = fmaf(pj, c, acc[g][2 * w + 1]);
-          }
+          row_axpy<T, DPL>(vr[j], pj, acc[g]);
         }
       }
     }
@@ -470,8 +502,8 @@ int decode_common(const void* q, const void* key_cache, const void* value_cache,
     set_error("decode_attention: only bf16 and fp16 are supported");
     return LPC_ERR_UNSUPPORTED;
   }
-  if (head_dim != 128 && head_dim != 64) {
-    set_error("decode_attention: head_dim must be 64 or 128, got %d", head_dim);
+  if (head_dim != 128 && head_dim != 64 && head_dim != 32) {
+    set_error("decode_attention: head_dim must be 32, 64 or 128, got %d", head_dim);
     return LPC_ERR_UNSUPPORTED;
   }
   if (!q || !key_cache || !value_cache || !seq_lens || !out) {
@@ -507,11 +539,15 @@ int decode_common(const void* q, const void* key_cache, const void* value_cache,
   if (dtype == LPC_DTYPE_BF16) {
     if (head_dim == 128)
       return launch_d<__nv_bfloat16, 128>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
-    return launch_d<__nv_bfloat16, 64>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
+    if (head_dim == 64)
+      return launch_d<__nv_bfloat16, 64>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
+    return launch_d<__nv_bfloat16, 32>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
   }
   if (head_dim == 128)
     return launch_d<__half, 128>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
-  return launch_d<__half, 64>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
+  if (head_dim == 64)
+    return launch_d<__half, 64>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
+  return launch_d<__half, 32>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
 }
 
 }  // namespace

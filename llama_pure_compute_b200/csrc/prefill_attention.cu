@@ -65,12 +65,15 @@ namespace {
 constexpr int BQ = 128;                   // queries per tile (UMMA M)
 constexpr int NQT = 2;                    // query tiles per CTA
 constexpr int BKV = 128;                  // keys per tile
-constexpr int HD = 128;                   // head dim
 constexpr int BOX = 64;                   // 64 x 2 B = one 128-byte swizzle row
-constexpr int TILE_BYTES = BQ * HD * 2;   // 32 KB: one Q tile, one K or V stage
-constexpr int HALF_BYTES = TILE_BYTES / 2;
+constexpr int HALF_BYTES = BQ * BOX * 2;  // 16 KB: 128 rows x one 64-column box
 constexpr int KV_STAGES = 2;
-constexpr int SMEM_BYTES = (NQT + 2 * KV_STAGES) * TILE_BYTES + 1024 + 256;
+// head_dim HD (64 or 128): a Q tile, a K stage and a V stage are HD / 64
+// boxes of 128 rows x 64 columns
+template <int HD>
+constexpr int tile_bytes() { return (HD / BOX) * HALF_BYTES; }
+template <int HD>
+constexpr int smem_bytes() { return (NQT + 2 * KV_STAGES) * tile_bytes<HD>() + 1024 + 256; }
 constexpr int NTHREADS = 384;  // 2 softmax warpgroups + 1 load/MMA warpgroup
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float LOG2E = 1.4426950408889634f;
@@ -180,11 +183,13 @@ constexpr int SPLIT_REGS_LOADMMA = 96, SPLIT_REGS_SOFTMAX = 200;
 static_assert(128 * SPLIT_REGS_LOADMMA + 256 * SPLIT_REGS_SOFTMAX <= NTHREADS * LAUNCH_REGS,
               "register split exceeds the block's launch allocation");
 
-template <typename T>
+template <typename T, int HD>
 __global__ void __launch_bounds__(NTHREADS, 1)
     flash_prefill_kernel(const __grid_constant__ TmaDesc4 tmQ, const __grid_constant__ TmaDesc4 tmK,
                          const __grid_constant__ TmaDesc4 tmV, T* __restrict__ out,
                          const Params p, uint32_t idesc_qk, uint32_t idesc_pv) {
+  constexpr int TILE_BYTES = tile_bytes<HD>();
+  constexpr int NBOX = HD / BOX;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = lpc::smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -262,23 +267,27 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int kvh = it.h / p.group;
         if (!(ok = lpc::mbar_wait(q_empty, ((uint32_t)r & 1u) ^ 1u, st))) break;
         lpc::mbar_arrive_expect_tx(q_full, NQT * TILE_BYTES);
-        for (int t = 0; t < NQT; ++t) {
-          tma_load_4d(sQ + t * TILE_BYTES, &tmQ, 0, (int)(it.q0 + t * BQ), it.h, it.b, q_full);
-          tma_load_4d(sQ + t * TILE_BYTES + HALF_BYTES, &tmQ, BOX, (int)(it.q0 + t * BQ), it.h,
-                      it.b, q_full);
-        }
+        for (int t = 0; t < NQT; ++t)
+#pragma unroll
+          for (int hb = 0; hb < NBOX; ++hb)
+            tma_load_4d(sQ + t * TILE_BYTES + hb * HALF_BYTES, &tmQ, hb * BOX,
+                        (int)(it.q0 + t * BQ), it.h, it.b, q_full);
         for (int j = 0; j < it.n1; ++j, ++kvc) {
           const int s = kvc % KV_STAGES;
           const uint32_t par = ((kvc / KV_STAGES) & 1u) ^ 1u;
           const int k0 = j * BKV;
           if (!(ok = lpc::mbar_wait(k_empty(s), par, st))) break;
           lpc::mbar_arrive_expect_tx(k_full(s), TILE_BYTES);
-          tma_load_4d(sK + s * TILE_BYTES, &tmK, 0, k0, kvh, it.b, k_full(s));
-          tma_load_4d(sK + s * TILE_BYTES + HALF_BYTES, &tmK, BOX, k0, kvh, it.b, k_full(s));
+#pragma unroll
+          for (int hb = 0; hb < NBOX; ++hb)
+            tma_load_4d(sK + s * TILE_BYTES + hb * HALF_BYTES, &tmK, hb * BOX, k0, kvh, it.b,
+                        k_full(s));
           if (!(ok = lpc::mbar_wait(v_empty(s), par, st))) break;
           lpc::mbar_arrive_expect_tx(v_full(s), TILE_BYTES);
-          tma_load_4d(sV + s * TILE_BYTES, &tmV, 0, k0, kvh, it.b, v_full(s));
-          tma_load_4d(sV + s * TILE_BYTES + HALF_BYTES, &tmV, BOX, k0, kvh, it.b, v_full(s));
+#pragma unroll
+          for (int hb = 0; hb < NBOX; ++hb)
+            tma_load_4d(sV + s * TILE_BYTES + hb * HALF_BYTES, &tmV, hb * BOX, k0, kvh, it.b,
+                        v_full(s));
         }
       }
     }
@@ -564,6 +573,30 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
 }
 
+// The kernel's setmaxnreg split is sized for LAUNCH_REGS registers per
+// thread: with fewer, the softmax warpgroups' increase could never be granted,
+// so any other count refuses to launch.
+template <typename T, int HD>
+int launch_prefill(dim3 grid, const TmaDesc4& tq, const TmaDesc4& tk, const TmaDesc4& tv,
+                   void* out, const Params& p, uint32_t id_qk, uint32_t id_pv, cudaStream_t s) {
+  static int regs = 0;
+  if (regs == 0) {
+    cudaFuncAttributes fa;
+    regs = cudaFuncGetAttributes(&fa, flash_prefill_kernel<T, HD>) == cudaSuccess ? fa.numRegs : -1;
+  }
+  if (regs != LAUNCH_REGS) {
+    lpc::set_error("flash_attention: kernel built with %d registers per thread, its register "
+                   "split needs %d", regs, LAUNCH_REGS);
+    return LPC_ERR_UNSUPPORTED;
+  }
+  constexpr int smem = smem_bytes<HD>();
+  static std::atomic<uint64_t> mask{0};
+  if (int rc = lpc::once_per_device_smem((const void*)flash_prefill_kernel<T, HD>, smem, mask))
+    return rc;
+  flash_prefill_kernel<T, HD><<<grid, NTHREADS, smem, s>>>(tq, tk, tv, (T*)out, p, id_qk, id_pv);
+  return LPC_OK;
+}
+
 }  // namespace
 
 extern "C" int lpc_flash_attention(const void* q, const void* k, const void* v, void* out,
@@ -583,8 +616,9 @@ extern "C" int lpc_flash_attention(const void* q, const void* k, const void* v, 
     set_error("flash_attention: Q_LEN cannot exceed KV_LEN.");
     return LPC_ERR_INVALID;
   }
-  if (head_dim != HD) {
-    set_error("flash_attention: head_dim %d not supported by the tcgen05 kernel (128)", head_dim);
+  if (head_dim != 128 && head_dim != 64) {
+    set_error("flash_attention: head_dim %d not supported by the tcgen05 kernel (64 or 128)",
+              head_dim);
     return LPC_ERR_UNSUPPORTED;
   }
   if (dtype != LPC_DTYPE_BF16 && dtype != LPC_DTYPE_F16) {
@@ -641,39 +675,18 @@ extern "C" int lpc_flash_attention(const void* q, const void* k, const void* v, 
   p.causal = causal ? 1 : 0;
   const uint32_t fmt = dtype == LPC_DTYPE_BF16 ? 1u : 0u;
   const uint32_t id_qk = idesc_f16(fmt, BQ, BKV, 0u, 0u);
-  const uint32_t id_pv = idesc_f16(fmt, BQ, HD, 0u, 1u);
+  const uint32_t id_pv = idesc_f16(fmt, BQ, (uint32_t)head_dim, 0u, 1u);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // persistent: one CTA per SM loops over the work items
   dim3 grid((unsigned)std::min<int64_t>(items, current_device_sms()));
   int rc;
-  // the kernel's setmaxnreg split is sized for LAUNCH_REGS registers per thread:
-  // with fewer, the softmax warpgroups' increase could never be granted
-  {
-    static int regs[2] = {0, 0};
-    const int ti = dtype == LPC_DTYPE_BF16 ? 0 : 1;
-    if (regs[ti] == 0) {
-      cudaFuncAttributes fa;
-      const cudaError_t e = dtype == LPC_DTYPE_BF16
-                                ? cudaFuncGetAttributes(&fa, flash_prefill_kernel<__nv_bfloat16>)
-                                : cudaFuncGetAttributes(&fa, flash_prefill_kernel<__half>);
-      regs[ti] = e == cudaSuccess ? fa.numRegs : -1;
-    }
-    if (regs[ti] != LAUNCH_REGS) {
-      set_error("flash_attention: kernel built with %d registers per thread, its register split "
-                "needs %d", regs[ti], LAUNCH_REGS);
-      return LPC_ERR_UNSUPPORTED;
-    }
-  }
   if (dtype == LPC_DTYPE_BF16) {
-    static std::atomic<uint64_t> mask{0};
-    if ((rc = once_per_device_smem((const void*)flash_prefill_kernel<__nv_bfloat16>, SMEM_BYTES, mask)))
-      return rc;
-    flash_prefill_kernel<__nv_bfloat16><<<grid, NTHREADS, SMEM_BYTES, s>>>(tq, tk, tv, (__nv_bfloat16*)out, p, id_qk, id_pv);
+    rc = head_dim == 128 ? launch_prefill<__nv_bfloat16, 128>(grid, tq, tk, tv, out, p, id_qk, id_pv, s)
+                         : launch_prefill<__nv_bfloat16, 64>(grid, tq, tk, tv, out, p, id_qk, id_pv, s);
   } else {
-    static std::atomic<uint64_t> mask{0};
-    if ((rc = once_per_device_smem((const void*)flash_prefill_kernel<__half>, SMEM_BYTES, mask)))
-      return rc;
-    flash_prefill_kernel<__half><<<grid, NTHREADS, SMEM_BYTES, s>>>(tq, tk, tv, (__half*)out, p, id_qk, id_pv);
+    rc = head_dim == 128 ? launch_prefill<__half, 128>(grid, tq, tk, tv, out, p, id_qk, id_pv, s)
+                         : launch_prefill<__half, 64>(grid, tq, tk, tv, out, p, id_qk, id_pv, s);
   }
+  if (rc) return rc;
   return check_launch("flash_attention");
 }

@@ -36,6 +36,7 @@
 //   dot products per warp.  It is the weight-streaming (HBM-bound) GEMV of the
 //   fp32 op shape (8 tokens).
 #include <algorithm>
+#include <type_traits>
 #include <atomic>
 #include <mutex>
 
@@ -250,6 +251,28 @@ struct PairGeom {
 template <int WMAX, int STAGES>
 constexpr int pair_smem() { return STAGES * PairGeom<WMAX>::STAGE + 1024 + 256; }
 
+// Sum of squares of the 8 elements of a 16-byte chunk (fixed order).
+template <typename T>
+__device__ __forceinline__ float sumsq8(const uint4& u) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float a, b;
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      a = lpc::bf16lo(w[i]);
+      b = lpc::bf16hi(w[i]);
+    } else {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      a = f.x;
+      b = f.y;
+    }
+    s = fmaf(a, a, s);
+    s = fmaf(b, b, s);
+  }
+  return s;
+}
+
 // Inter tile c of C covers columns [pair_col(c), pair_col(c + 1)): the I / 16
 // sixteen-column units dealt out as evenly as possible, so tile widths differ
 // by at most 16 and C can be matched to the number of CTA pairs per wave.
@@ -262,12 +285,20 @@ __host__ __device__ __forceinline__ int pair_col(int c, int units, int C) {
 // col0 + r*w/2 .. (w/2 gate rows, w/2 up rows) of each k-block; rank 0 issues
 // an M=256, N=w MMA for gate (TMEM columns 0..w-1) and one for up (columns
 // w..2w-1), each CTA receiving its own 128 token rows.
-template <typename T, int WMAX, int STAGES>
+//
+// NORM: A holds the raw rows x of the RMSNorm and the gate/up weights come
+// with the norm weight folded in (W diag(w)).  Each MMA commits to a
+// `consumed` barrier; the epilogue warps -- one per 32 token rows, idle until
+// the accumulators are ready -- then read their token row of the stage's A
+// tile, accumulate its sum of squares and release the stage (its `empty`
+// barrier counts their four arrivals).  The epilogue scales each token's
+// gate and up accumulators by rsqrt(sum / K + eps) before SiLU(g) * u.
+template <typename T, int WMAX, int STAGES, bool NORM>
 __global__ void __launch_bounds__(192)
     swiglu_pair_kernel(const __grid_constant__ lpc::TmaDesc tmA,
                        const __grid_constant__ lpc::TmaDesc tmG,
                        const __grid_constant__ lpc::TmaDesc tmU, T* __restrict__ out, int M, int K,
-                       int I, int up_row_off, int num_m, int num_c, uint32_t ab_fmt) {
+                       int I, int up_row_off, int num_m, int num_c, uint32_t ab_fmt, float eps) {
   constexpr uint32_t TMEM_COLS = 512;
   constexpr int PAIR_B_BYTES = PairGeom<WMAX>::B_BYTES;
   constexpr int PAIR_STAGE = PairGeom<WMAX>::STAGE;
@@ -280,9 +311,13 @@ __global__ void __launch_bounds__(192)
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
   const uint32_t accum_bar = bars + 8u * (2 * STAGES);
-  const uint32_t tmem_slot = accum_bar + 8u;
+  auto consumed_bar = [&](int s) { return bars + 8u * (2 * STAGES + 1 + s); };  // NORM only
+  const uint32_t tmem_slot = bars + 8u * (3 * STAGES + 1);
   volatile uint32_t* tmem_slot_ptr =
       reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
+  // the MMA's completion of a stage: straight to `empty`, or with NORM to
+  // `consumed`, after which the epilogue warps read the A rows and release it
+  auto mma_done_bar = [&](int s) { return NORM ? consumed_bar(s) : empty_bar(s); };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = lpc::cluster_ctarank();
@@ -301,7 +336,8 @@ __global__ void __launch_bounds__(192)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       lpc::mbar_init(full_bar(s), 1);
-      lpc::mbar_init(empty_bar(s), 1);
+      lpc::mbar_init(empty_bar(s), NORM ? 4 : 1);
+      if (NORM) lpc::mbar_init(consumed_bar(s), 1);
     }
     lpc::mbar_init(accum_bar, 1);
     lpc::fence_mbar_init();
@@ -360,7 +396,7 @@ __global__ void __launch_bounds__(192)
     if (lane == 0) {
       if (rank == 0) {
         const uint32_t idesc = lpc::idesc_f16(ab_fmt, PAIR_TOK, (uint32_t)w, 0u, 0u);
-        const uint32_t peer_empty0 = lpc::mapa_shared(empty_bar(0), 1);
+        const uint32_t peer_done0 = lpc::mapa_shared(mma_done_bar(0), 1);
         const uint32_t peer_accum = lpc::mapa_shared(accum_bar, 1);
         for (int kb = 0; kb < nkb; ++kb) {
           const int s = kb % STAGES;
@@ -376,8 +412,8 @@ __global__ void __launch_bounds__(192)
             lpc::umma_ss_pair(tmem, ad + 2u * kk, gd + 2u * kk, idesc, (kb | kk) != 0);
             lpc::umma_ss_pair(tmem + (uint32_t)w, ad + 2u * kk, ud + 2u * kk, idesc, (kb | kk) != 0);
           }
-          lpc::umma_commit_pair(empty_bar(s));
-          lpc::umma_commit_pair(peer_empty0 + 8u * s);
+          lpc::umma_commit_pair(mma_done_bar(s));
+          lpc::umma_commit_pair(peer_done0 + 8u * s);
         }
         lpc::umma_commit_pair(accum_bar);
         lpc::umma_commit_pair(peer_accum);
@@ -386,7 +422,38 @@ __global__ void __launch_bounds__(192)
   } else {
     // epilogue warps 0..3: TMEM lanes 32*warp .. +31 = this CTA's tokens;
     // columns 0..w-1 gate, w..2w-1 up, for inter columns col0 ..
-    const bool ok = lpc::mbar_wait(accum_bar, 0, st);
+    bool stats_ok = true;
+    float rs = 1.f;  // NORM: this token row's rsqrt(mean(x^2) + eps)
+    if (NORM) {
+      const int trow = warp * 32 + lane;  // row of this CTA's A tile
+      float ss = 0.f;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % STAGES;
+        // one lane per warp waits; the warp follows it
+        bool got = true;
+        if (lane == 0) got = lpc::mbar_wait(consumed_bar(s), (uint32_t)(kb / STAGES) & 1u, st);
+        if (!__shfl_sync(0xffffffffu, got, 0)) {
+          stats_ok = false;
+          break;
+        }
+        const uint32_t ra = sA + s * A_BYTES + (uint32_t)trow * 128u;
+        // lane l starts at chunk l % 8: the 8 lanes of a quarter-warp read 8
+        // different 16-byte chunks (all 32 banks) instead of the same one
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 u;
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
+                       : "r"(ra + (uint32_t)(((c + lane) & 7) * 16))
+                       : "memory");
+          ss += sumsq8<T>(u);
+        }
+        __syncwarp();
+        if (lane == 0) lpc::mbar_arrive(empty_bar(s));
+      }
+      rs = rsqrtf(ss / (float)K + eps);
+    }
+    const bool ok = lpc::mbar_wait(accum_bar, 0, st) && stats_ok;
     lpc::tc_fence_after();
     if (ok) {
       const int row = m0 + warp * 32 + lane;
@@ -401,8 +468,9 @@ __global__ void __launch_bounds__(192)
           uint32_t p[8];
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            p[j] = pack2<T>(silu_mul(__uint_as_float(g[2 * j]), __uint_as_float(u[2 * j])),
-                            silu_mul(__uint_as_float(g[2 * j + 1]), __uint_as_float(u[2 * j + 1])));
+            p[j] = pack2<T>(silu_mul(__uint_as_float(g[2 * j]) * rs, __uint_as_float(u[2 * j]) * rs),
+                            silu_mul(__uint_as_float(g[2 * j + 1]) * rs,
+                                     __uint_as_float(u[2 * j + 1]) * rs));
           uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)row * I + col0 + c);
           dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
           dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
@@ -546,30 +614,10 @@ __global__ void __launch_bounds__(F32_WARPS * 32, 1)
       const float* r[4];
       unit_rows(rp0 + pl, r);
       const int va = (int)((int64_t)kp * kv / F32_KPARTS), vb = (int)((int64_t)(kp + 1) * kv / F32_KPARTS);
-      {
-        // L2 prefetch of this warp's unit after the next (the first two were
-        // prefetched under the prologue): keeps DRAM requests in flight while
-        // the loads of this unit wait on L2 hits
-        const int un = u + 2 * F32_WARPS;
-        if (rp0 + un / F32_KPARTS < p_end) {
-          const float* rn[4];
-          unit_rows(rp0 + un / F32_KPARTS, rn);
-          const int kq = un % F32_KPARTS;
-          const int64_t k0 = (int64_t)kq * kv / F32_KPARTS * 4, k1 = (int64_t)(kq + 1) * kv / F32_KPARTS * 4;
-          for (int64_t k = k0 + lane * 32; k < k1; k += 32 * 32) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) asm volatile("prefetch.global.L2 [%0];" ::"l"(rn[j] + k));
-          }
-        }
-      }
       float acc[32];  // [row j][token t] at 8 * j + t
 #pragma unroll
       for (int i = 0; i < 32; ++i) acc[i] = 0.f;
-#pragma unroll 2
-      for (int v = va + lane; v < vb; v += 32) {
-        float4 w[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) w[j] = __ldg(reinterpret_cast<const float4*>(r[j]) + v);
+      auto fma_step = [&](const float4 (&w)[4], int v) {
 #pragma unroll
         for (int t = 0; t < F32_ROWS; ++t) {
           const float4 a = xs4[(int64_t)t * kv + v];
@@ -582,6 +630,25 @@ __global__ void __launch_bounds__(F32_WARPS * 32, 1)
             s = fmaf(w[j].w, a.w, s);
             acc[8 * j + t] = s;
           }
+        }
+      };
+      if (vb - va == 4 * 32) {
+        // the common case (K = 4096): all 16 loads of the unit in flight at once
+        float4 w[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            w[i][j] = __ldg(reinterpret_cast<const float4*>(r[j]) + va + lane + 32 * i);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) fma_step(w[i], va + lane + 32 * i);
+      } else {
+#pragma unroll 2
+        for (int v = va + lane; v < vb; v += 32) {
+          float4 w[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) w[j] = __ldg(reinterpret_cast<const float4*>(r[j]) + v);
+          fma_step(w, v);
         }
       }
       const float tot = warp_transpose_sum32(acc, lane);
@@ -693,9 +760,9 @@ int64_t pair_tiles(int64_t num_m, int I, int wmax, int* num_c) {
   return best_cost;
 }
 
-template <typename T, int WMAX, int STAGES>
+template <typename T, int WMAX, int STAGES, bool NORM = false>
 int launch_pair(const lpc::TmaDesc& ta, const void* gw, const void* uw, void* out, int64_t M, int K,
-                int I, int dtype, cudaStream_t s) {
+                int I, int dtype, cudaStream_t s, float eps = 0.f) {
   constexpr int BROWS = PairGeom<WMAX>::BROWS;
   lpc::TmaDesc tg, tu;
   int rc, up_off = 0;
@@ -709,7 +776,7 @@ int launch_pair(const lpc::TmaDesc& ta, const void* gw, const void* uw, void* ou
   }
   constexpr int smem = pair_smem<WMAX, STAGES>();
   static std::atomic<uint64_t> mask{0};
-  if ((rc = lpc::once_per_device_smem((const void*)swiglu_pair_kernel<T, WMAX, STAGES>, smem, mask)))
+  if ((rc = lpc::once_per_device_smem((const void*)swiglu_pair_kernel<T, WMAX, STAGES, NORM>, smem, mask)))
     return rc;
   const int num_m = (int)((M + PAIR_TOK - 1) / PAIR_TOK);
   int num_c = 0;
@@ -730,9 +797,9 @@ int launch_pair(const lpc::TmaDesc& ta, const void* gw, const void* uw, void* ou
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, swiglu_pair_kernel<T, WMAX, STAGES>, ta, tg, tu, (T*)out,
-                                     (int)M, K, I, up_off, num_m, num_c,
-                                     dtype == LPC_DTYPE_BF16 ? 1u : 0u);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, swiglu_pair_kernel<T, WMAX, STAGES, NORM>, ta, tg, tu,
+                                     (T*)out, (int)M, K, I, up_off, num_m, num_c,
+                                     dtype == LPC_DTYPE_BF16 ? 1u : 0u, eps);
   if (e != cudaSuccess) {
     lpc::set_error("rmsswiglu_forward (tcgen05 pair): launch failed: %s", cudaGetErrorString(e));
     return LPC_ERR_CUDA;
@@ -741,15 +808,15 @@ int launch_pair(const lpc::TmaDesc& ta, const void* gw, const void* uw, void* ou
 }
 
 // The pair kernel with the cheaper of the 160- and 256-column tilings.
-template <typename T>
+template <typename T, bool NORM = false>
 int launch_pair_auto(const lpc::TmaDesc& ta, const void* gw, const void* uw, void* out, int64_t M,
-                     int K, int I, int dtype, cudaStream_t s) {
+                     int K, int I, int dtype, cudaStream_t s, float eps = 0.f) {
   const int64_t num_m = (M + PAIR_TOK - 1) / PAIR_TOK;
   int c160 = 0, c256 = 0;
   const int64_t cost160 = pair_tiles(num_m, I, 160, &c160);
   const int64_t cost256 = pair_tiles(num_m, I, 256, &c256);
-  if (cost256 < cost160) return launch_pair<T, 256, 4>(ta, gw, uw, out, M, K, I, dtype, s);
-  return launch_pair<T, 160, 5>(ta, gw, uw, out, M, K, I, dtype, s);
+  if (cost256 < cost160) return launch_pair<T, 256, 4, NORM>(ta, gw, uw, out, M, K, I, dtype, s, eps);
+  return launch_pair<T, 160, 5, NORM>(ta, gw, uw, out, M, K, I, dtype, s, eps);
 }
 
 template <typename T>
@@ -846,4 +913,46 @@ extern "C" int lpc_rmsswiglu_forward(const void* x, const void* rms_weight, cons
   if (dtype == LPC_DTYPE_BF16)
     return launch_tc<__nv_bfloat16>(workspace, gate_w, up_w, out, tokens, dim, inter, dtype, s);
   return launch_tc<__half>(workspace, gate_w, up_w, out, tokens, dim, inter, dtype, s);
+}
+
+// RMSNorm + SwiGLU in one kernel when the norm weight is already folded into
+// the gate/up weights (W diag(w), e.g. once at model load): the CTA-pair
+// kernel reads the raw rows x, takes each row's sum of squares from the A
+// tiles it feeds the tensor core and scales the accumulators in the epilogue.
+extern "C" int lpc_rmsswiglu_folded_forward(const void* x, const void* gate_w, const void* up_w,
+                                            void* out, int64_t tokens, int dim, int inter,
+                                            float eps, int dtype, void* stream) {
+  using namespace lpc;
+  if (!(eps > 0.f)) {
+    set_error("rmsswiglu_folded_forward: eps must be strictly positive.");
+    return LPC_ERR_INVALID;
+  }
+  if (tokens < 0 || dim <= 0 || inter <= 0) {
+    set_error("rmsswiglu_folded_forward: invalid sizes (tokens=%lld dim=%d inter=%d)",
+              (long long)tokens, dim, inter);
+    return LPC_ERR_INVALID;
+  }
+  if (tokens == 0) return LPC_OK;
+  if (dtype != LPC_DTYPE_BF16 && dtype != LPC_DTYPE_F16) {
+    set_error("rmsswiglu_folded_forward: bf16 or fp16 only");
+    return LPC_ERR_UNSUPPORTED;
+  }
+  if (dim % BK || inter % 16 || tokens > 0x7fffffffLL) {
+    set_error("rmsswiglu_folded_forward: needs dim %% 64 == 0 and inter %% 16 == 0 (dim=%d "
+              "inter=%d)", dim, inter);
+    return LPC_ERR_UNSUPPORTED;
+  }
+  if (!x || !gate_w || !out || !aligned16(x) || !aligned16(gate_w) || (up_w && !aligned16(up_w)) ||
+      !aligned16(out)) {
+    set_error("rmsswiglu_folded_forward: null or misaligned pointer");
+    return LPC_ERR_INVALID;
+  }
+  lpc::TmaDesc ta;
+  int rc = lpc::make_tma_2d(&ta, x, dtype, (uint64_t)dim, (uint64_t)tokens, (uint64_t)dim * 2, BK,
+                            BM, true);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == LPC_DTYPE_BF16)
+    return launch_pair_auto<__nv_bfloat16, true>(ta, gate_w, up_w, out, tokens, dim, inter, dtype, s, eps);
+  return launch_pair_auto<__half, true>(ta, gate_w, up_w, out, tokens, dim, inter, dtype, s, eps);
 }

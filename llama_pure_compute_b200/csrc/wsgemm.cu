@@ -87,6 +87,49 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
   return __fdividef(g, 1.0f + __expf(-g)) * u;
 }
 
+// Sum of squares of the 8 elements of a 16-byte chunk (fixed order).
+template <typename T>
+__device__ __forceinline__ float sumsq8(const uint4& u);
+template <>
+__device__ __forceinline__ float sumsq8<__nv_bfloat16>(const uint4& u) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float a = lpc::bf16lo(w[i]), b = lpc::bf16hi(w[i]);
+    s = fmaf(a, a, s);
+    s = fmaf(b, b, s);
+  }
+  return s;
+}
+template <>
+__device__ __forceinline__ float sumsq8<__half>(const uint4& u) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    s = fmaf(f.x, f.x, s);
+    s = fmaf(f.y, f.y, s);
+  }
+  return s;
+}
+
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 r;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "r"(addr)
+               : "memory");
+  return r;
+}
+
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float r;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(r) : "r"(addr) : "memory");
+  return r;
+}
+
 // ---------------------------------------------------------------------------
 // Packing: packed[tile][kb] = swizzled image of rows tile*128.. x k kb*64..
 // layout 0: row r of W0 (rows >= n_rows are zero)
@@ -101,6 +144,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 template <typename T>
 __global__ void __launch_bounds__(256) pack_kernel(const T* __restrict__ w0,
                                                    const T* __restrict__ w1,
+                                                   const float* __restrict__ kscale,
                                                    uint4* __restrict__ packed, int64_t n_rows,
                                                    int K, int n_tiles, int layout) {
   const int n_kb = K / KB;
@@ -132,7 +176,15 @@ __global__ void __launch_bounds__(256) pack_kernel(const T* __restrict__ w0,
         else src = w1 ? w1 + col * K + k : w0 + (n_rows + col) * K + k;
       }
     }
-    packed[idx] = src ? *reinterpret_cast<const uint4*>(src) : make_uint4(0, 0, 0, 0);
+    uint4 v = src ? *reinterpret_cast<const uint4*>(src) : make_uint4(0, 0, 0, 0);
+    if (src && kscale) {
+      // W[n, k] * scale[k] in fp32, one rounding (an RMSNorm weight folded
+      // into the projection that consumes the normalised rows)
+      T* e = reinterpret_cast<T*>(&v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) e[j] = Num<T>::from_f(Num<T>::to_f(e[j]) * __ldg(kscale + k + j));
+    }
+    packed[idx] = v;
   }
 }
 
@@ -269,9 +321,15 @@ __device__ __forceinline__ void emit_qkv(const float (&v)[CNT], const EpiPre<CNT
 // Epilogue of CNT accumulator columns (tokens c .. c+CNT-1) of this thread's
 // tile row (CNT in {4, 8, 16}); `pre` from epi_prefetch on the same columns.
 template <typename T, int EPI, int CNT>
-__device__ __forceinline__ void emit(const float (&v)[CNT], const EpiPre<CNT>& pre, T* out,
+__device__ __forceinline__ void emit(float (&v)[CNT], const EpiPre<CNT>& pre, T* out,
                                      int M, int n_out, int tile, int q, int lane, int c,
-                                     const QkvArgs& qa, const TokSlot* tab) {
+                                     const QkvArgs& qa, const TokSlot* tab, const float* rt) {
+  if (rt) {
+    // fused RMSNorm: the accumulator holds x . (W * w); scale by the token
+    // row's rsqrt(mean(x^2) + eps)
+#pragma unroll
+    for (int i = 0; i < CNT; ++i) v[i] *= rt[c + i];
+  }
   if (EPI == EPI_QKV) {
     emit_qkv<T, CNT>(v, pre, qa, tab, M, tile, q, lane, c);
   } else if (EPI == EPI_SWIGLU) {
@@ -327,7 +385,8 @@ __device__ __forceinline__ float4 ld_cluster_v4(uint32_t addr) {
 template <typename T, int EPI, int S, int C>
 __device__ __forceinline__ void reduce_slice(uint32_t prow, int swz, int c0, int width, T* out,
                                              const T* resid, int M, int n_out, int tile, int q,
-                                             int lane, const QkvArgs& qa, const TokSlot* tab) {
+                                             int lane, const QkvArgs& qa, const TokSlot* tab,
+                                             const float* rt) {
   constexpr int G = C / 4;
   uint32_t peer[S];
 #pragma unroll
@@ -358,7 +417,7 @@ __device__ __forceinline__ void reduce_slice(uint32_t prow, int swz, int c0, int
         v[4 * g + 3] += buf[g][k].w;
       }
     }
-    emit<T, EPI, C>(v, pre, out, M, n_out, tile, q, lane, c, qa, tab);
+    emit<T, EPI, C>(v, pre, out, M, n_out, tile, q, lane, c, qa, tab, rt);
   }
 }
 
@@ -368,20 +427,20 @@ template <typename T, int EPI, int S>
 __device__ __forceinline__ void reduce_slice_any(uint32_t prow, int swz, int c0, int width,
                                                  T* out, const T* resid, int M, int n_out,
                                                  int tile, int q, int lane, const QkvArgs& qa,
-                                                 const TokSlot* tab) {
+                                                 const TokSlot* tab, const float* rt) {
   if constexpr (S <= 2) {
     if (width % 16 == 0) {
-      reduce_slice<T, EPI, S, 16>(prow, swz, c0, width, out, resid, M, n_out, tile, q, lane, qa, tab);
+      reduce_slice<T, EPI, S, 16>(prow, swz, c0, width, out, resid, M, n_out, tile, q, lane, qa, tab, rt);
       return;
     }
   }
   if constexpr (S <= 4) {
     if (width % 8 == 0) {
-      reduce_slice<T, EPI, S, 8>(prow, swz, c0, width, out, resid, M, n_out, tile, q, lane, qa, tab);
+      reduce_slice<T, EPI, S, 8>(prow, swz, c0, width, out, resid, M, n_out, tile, q, lane, qa, tab, rt);
       return;
     }
   }
-  reduce_slice<T, EPI, S, 4>(prow, swz, c0, width, out, resid, M, n_out, tile, q, lane, qa, tab);
+  reduce_slice<T, EPI, S, 4>(prow, swz, c0, width, out, resid, M, n_out, tile, q, lane, qa, tab, rt);
 }
 
 // splits > 1: the kernel runs in clusters of `splits` CTAs, one weight tile
@@ -392,11 +451,20 @@ __device__ __forceinline__ void reduce_slice_any(uint32_t prow, int swz, int c0,
 // distributed shared memory and runs the epilogue on them.  A second cluster
 // barrier keeps every CTA's shared memory alive until all slices are read.
 // No atomics, no global workspace.
-template <typename T, int EPI>
+//
+// NORM: the activations are the raw rows x of an RMSNorm whose weight is
+// folded into the packed weights (lpc_pack_weights' k_scale).  While the main
+// loop runs, the epilogue warps read every activation tile the MMA consumes
+// from shared memory and accumulate each token row's sum of squares (the
+// stage is released only after both the MMA and these reads are done); the
+// split ranks add their partial sums through distributed shared memory, and
+// the epilogue multiplies each token's accumulators by rsqrt(sum / K + eps):
+// norm(x) W^T = rsqrt(mean(x^2) + eps) * (x (W diag(w))^T).
+template <typename T, int EPI, bool NORM>
 __global__ void __launch_bounds__(THREADS, 2)
     wsgemm_kernel(const __grid_constant__ lpc::TmaDesc tmX, const uint8_t* __restrict__ packed,
                   T* out, const T* resid, int M, int K, int n_out, int NT, int stages,
-                  uint32_t tmem_cols, uint32_t idesc, int splits, const QkvArgs qa) {
+                  uint32_t tmem_cols, uint32_t idesc, int splits, const QkvArgs qa, float eps) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = lpc::smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -409,8 +477,12 @@ __global__ void __launch_bounds__(THREADS, 2)
   const uint32_t tmem_slot = accum + 8u;
   volatile uint32_t* tmem_slot_ptr =
       reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
-  // EPI_QKV token table (TOK_TABLE_BYTES past the barriers)
+  // EPI_QKV token table (TOK_TABLE_BYTES past the barriers), then for NORM
+  // the per-token sums of squares and row scales (MAX_TOKENS floats each)
   TokSlot* tab = reinterpret_cast<TokSlot*>(smem_raw + (tmem_slot + 16u - raw));
+  const uint32_t ssq_addr = tmem_slot + 16u + (EPI == EPI_QKV ? (uint32_t)TOK_TABLE_BYTES : 0u);
+  float* ssq = reinterpret_cast<float*>(smem_raw + (ssq_addr - raw));
+  float* rt = ssq + MAX_TOKENS;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = (int)blockIdx.x / splits;
@@ -435,7 +507,9 @@ __global__ void __launch_bounds__(THREADS, 2)
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       lpc::mbar_init(full_bar(s), 1);
-      lpc::mbar_init(empty_bar(s), 1);
+      // a stage is free once the MMA has read it, and with NORM once the four
+      // epilogue warps have read its activation rows
+      lpc::mbar_init(empty_bar(s), NORM ? 5 : 1);
     }
     lpc::mbar_init(accum, 1);
     lpc::fence_mbar_init();
@@ -497,8 +571,54 @@ __global__ void __launch_bounds__(THREADS, 2)
       build_token_table(tab, qa, M, (int)threadIdx.x - 128);
       asm volatile("bar.sync 1, 128;" ::: "memory");
     }
-    const bool ok = lpc::mbar_wait(accum, 0, st);
+    bool stats_ok = true;
+    if (NORM) {
+      // thread t reads 16-byte chunk t % 8 of token rows t / 8 + 16 j of
+      // every activation tile (rows are 128 bytes; the swizzle only permutes
+      // chunks within a row, so the row sums are unaffected)
+      const int tid = (int)threadIdx.x - 128;
+      const int pch = tid & 7, r0 = tid >> 3;
+      const int nrow = NT >> 4;
+      float acc[MAX_TOKENS / 16];
+#pragma unroll
+      for (int j = 0; j < MAX_TOKENS / 16; ++j) acc[j] = 0.f;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % stages;
+        // one lane per warp waits (a warp of pollers would contend with the
+        // producer and the MMA issuer for the barrier); the warp follows it
+        bool got = true;
+        if (lane == 0) got = lpc::mbar_wait(full_bar(s), (uint32_t)(i / stages) & 1u, st);
+        if (!__shfl_sync(0xffffffffu, got, 0)) {
+          stats_ok = false;
+          break;
+        }
+        const uint32_t xb = base + (uint32_t)s * stage_bytes + CHUNK + (uint32_t)(pch * 16 + r0 * 128);
+#pragma unroll
+        for (int j = 0; j < MAX_TOKENS / 16; ++j)
+          if (j < nrow) acc[j] += sumsq8<T>(ld_shared_v4(xb + (uint32_t)(j * 16 * 128)));
+        __syncwarp();
+        if (lane == 0) lpc::mbar_arrive(empty_bar(s));
+      }
+#pragma unroll
+      for (int j = 0; j < MAX_TOKENS / 16; ++j) {
+        acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], 1);
+        acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], 2);
+        acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], 4);
+      }
+      if (pch == 0) {
+#pragma unroll
+        for (int j = 0; j < MAX_TOKENS / 16; ++j)
+          if (j < nrow) ssq[r0 + 16 * j] = acc[j];
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (splits == 1) {
+        for (int t = tid; t < NT; t += 128) rt[t] = rsqrtf(ssq[t] / (float)K + eps);
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
+    }
+    const bool ok = lpc::mbar_wait(accum, 0, st) && stats_ok;
     lpc::tc_fence_after();
+    const float* rtp = NORM ? rt : nullptr;
     if (splits == 1) {
       if (ok) {
 #pragma unroll 1
@@ -511,7 +631,7 @@ __global__ void __launch_bounds__(THREADS, 2)
           float v[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-          emit<T, EPI, 16>(v, pre, out, M, n_out, tile, q, lane, c, qa, tab);
+          emit<T, EPI, 16>(v, pre, out, M, n_out, tile, q, lane, c, qa, tab, rtp);
         }
       }
     } else {
@@ -538,17 +658,29 @@ __global__ void __launch_bounds__(THREADS, 2)
                        : "memory");
       }
       __syncwarp();
-      lpc::cluster_sync();  // every rank's partial tile is in its shared memory
+      lpc::cluster_sync();  // every rank's partial tile (and sums of squares) is in its shared memory
+      if (NORM) {
+        // each token's sum of squares over all of K: the ranks' partial
+        // sums added in rank order
+        const int tid = (int)threadIdx.x - 128;
+        for (int t = tid; t < NT; t += 128) {
+          float tot = 0.f;
+          for (int k = 0; k < splits; ++k)
+            tot += ld_cluster_f32(lpc::mapa_shared(ssq_addr + (uint32_t)t * 4u, (uint32_t)k));
+          rt[t] = rsqrtf(tot / (float)K + eps);
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
       const int width = NT / splits;  // token columns reduced by this rank
       const int c0 = rank * width;
       switch (splits) {
 #define LPC_RS(S_)                                                                            \
   case S_:                                                                                    \
     reduce_slice_any<T, EPI, S_>(prow, swz, c0, width, out, resid, M, n_out, tile, q, lane, qa, \
-                                 tab);                                                        \
+                                 tab, rtp);                                                   \
     break;
         LPC_RS(2) LPC_RS(3) LPC_RS(4) LPC_RS(5) LPC_RS(6) LPC_RS(7)
-        default: reduce_slice_any<T, EPI, 8>(prow, swz, c0, width, out, resid, M, n_out, tile, q, lane, qa, tab); break;
+        default: reduce_slice_any<T, EPI, 8>(prow, swz, c0, width, out, resid, M, n_out, tile, q, lane, qa, tab, rtp); break;
 #undef LPC_RS
       }
     }
@@ -601,15 +733,20 @@ int choose_splits(const Plan& p, int K) {
   return 1;
 }
 
-Plan make_plan(int64_t M, int64_t n_out, int K, int epilogue) {
+constexpr int NORM_BYTES = 2 * MAX_TOKENS * (int)sizeof(float);  // sums of squares + row scales
+
+Plan make_plan(int64_t M, int64_t n_out, int K, int epilogue, bool norm) {
   Plan p;
   p.n_tiles = (int)(epilogue == EPI_SWIGLU ? (n_out + 63) / 64 : (n_out + TILE_ROWS - 1) / TILE_ROWS);
   p.NT = (int)((M + 15) / 16) * 16;
   const int stage_bytes = CHUNK + ((p.NT * KB * 2 + 1023) & ~1023);
   p.stages = std::max(2, std::min(8, SMEM_TARGET / stage_bytes));
-  // EPI_QKV keeps a per-token table after the barriers
-  const int extra = epilogue == EPI_QKV ? TOK_TABLE_BYTES : 0;
-  if (extra) p.stages = std::max(2, std::min(8, (SMEM_TARGET - extra) / stage_bytes));
+  // EPI_QKV keeps a per-token table after the barriers, NORM the per-token
+  // sums of squares and scales; they use the headroom above SMEM_TARGET as
+  // long as two CTAs still fit an SM (113 KB each)
+  const int extra = (epilogue == EPI_QKV ? TOK_TABLE_BYTES : 0) + (norm ? NORM_BYTES : 0);
+  while (p.stages > 2 && p.stages * stage_bytes + 1024 + 8 * (2 * p.stages + 4) + extra > 113 * 1024)
+    --p.stages;
   p.smem = p.stages * stage_bytes + 1024 + 8 * (2 * p.stages + 4) + extra;
   p.tmem_cols = 32;
   while ((int)p.tmem_cols < p.NT) p.tmem_cols <<= 1;
@@ -617,16 +754,17 @@ Plan make_plan(int64_t M, int64_t n_out, int K, int epilogue) {
   return p;
 }
 
-template <typename T, int EPI>
+template <typename T, int EPI, bool NORM>
 int launch(const void* x, const void* packed, void* out, const void* resid, int64_t M,
-           int64_t n_out, int K, int dtype, cudaStream_t s, const QkvArgs& qa = QkvArgs{}) {
-  const Plan p = make_plan(M, n_out, K, EPI);
+           int64_t n_out, int K, int dtype, cudaStream_t s, float eps,
+           const QkvArgs& qa = QkvArgs{}) {
+  const Plan p = make_plan(M, n_out, K, EPI, NORM);
   lpc::TmaDesc tx;
   int rc = lpc::make_tma_2d(&tx, x, dtype, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, KB,
                             (uint32_t)p.NT, true);
   if (rc) return rc;
   static std::atomic<uint64_t> mask{0};
-  if ((rc = lpc::once_per_device_smem((const void*)wsgemm_kernel<T, EPI>, 227 * 1024, mask)))
+  if ((rc = lpc::once_per_device_smem((const void*)wsgemm_kernel<T, EPI, NORM>, 227 * 1024, mask)))
     return rc;
   const uint32_t idesc =
       lpc::idesc_f16(dtype == LPC_DTYPE_BF16 ? 1u : 0u, TILE_ROWS, (uint32_t)p.NT, 0u, 0u);
@@ -646,9 +784,9 @@ int launch(const void* x, const void* packed, void* out, const void* resid, int6
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = p.splits > 1 ? 2 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, wsgemm_kernel<T, EPI>, tx, (const uint8_t*)packed,
+  cudaError_t e = cudaLaunchKernelEx(&cfg, wsgemm_kernel<T, EPI, NORM>, tx, (const uint8_t*)packed,
                                      (T*)out, (const T*)resid, (int)M, K, (int)n_out, p.NT,
-                                     p.stages, p.tmem_cols, idesc, p.splits, qa);
+                                     p.stages, p.tmem_cols, idesc, p.splits, qa, eps);
   if (e != cudaSuccess) {
     lpc::set_error("wsgemm (%d-way split): launch failed: %s", p.splits, cudaGetErrorString(e));
     return LPC_ERR_CUDA;
@@ -656,13 +794,13 @@ int launch(const void* x, const void* packed, void* out, const void* resid, int6
   return lpc::check_launch("wsgemm");
 }
 
-template <typename T>
+template <typename T, bool NORM>
 int launch_epi(int epilogue, const void* x, const void* packed, void* out, const void* resid,
-               int64_t M, int64_t n_out, int K, int dtype, cudaStream_t s) {
+               int64_t M, int64_t n_out, int K, int dtype, cudaStream_t s, float eps) {
   switch (epilogue) {
-    case EPI_STORE: return launch<T, EPI_STORE>(x, packed, out, resid, M, n_out, K, dtype, s);
-    case EPI_RESIDUAL: return launch<T, EPI_RESIDUAL>(x, packed, out, resid, M, n_out, K, dtype, s);
-    case EPI_SWIGLU: return launch<T, EPI_SWIGLU>(x, packed, out, resid, M, n_out, K, dtype, s);
+    case EPI_STORE: return launch<T, EPI_STORE, NORM>(x, packed, out, resid, M, n_out, K, dtype, s, eps);
+    case EPI_RESIDUAL: return launch<T, EPI_RESIDUAL, NORM>(x, packed, out, resid, M, n_out, K, dtype, s, eps);
+    case EPI_SWIGLU: return launch<T, EPI_SWIGLU, NORM>(x, packed, out, resid, M, n_out, K, dtype, s, eps);
   }
   lpc::set_error("wsgemm: unknown epilogue %d", epilogue);
   return LPC_ERR_INVALID;
@@ -677,8 +815,8 @@ extern "C" int64_t lpc_packed_weight_bytes(int64_t n_out, int k, int layout) {
   return tiles * (k / KB) * (int64_t)CHUNK;
 }
 
-extern "C" int lpc_pack_weights(const void* w0, const void* w1, void* packed, int64_t n_out, int k,
-                                int layout, int dtype, void* stream) {
+extern "C" int lpc_pack_weights(const void* w0, const void* w1, const float* k_scale, void* packed,
+                                int64_t n_out, int k, int layout, int dtype, void* stream) {
   using namespace lpc;
   if (n_out <= 0 || k <= 0 || k % KB || layout < 0 || layout > 2 ||
       (layout == 2 && n_out % HEAD_DIM)) {
@@ -700,10 +838,10 @@ extern "C" int lpc_pack_weights(const void* w0, const void* w1, void* packed, in
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == LPC_DTYPE_BF16)
     pack_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>((const __nv_bfloat16*)w0, (const __nv_bfloat16*)w1,
-                                                      (uint4*)packed, n_out, k, n_tiles, layout);
+                                                      k_scale, (uint4*)packed, n_out, k, n_tiles, layout);
   else
-    pack_kernel<__half><<<blocks, 256, 0, s>>>((const __half*)w0, (const __half*)w1, (uint4*)packed,
-                                               n_out, k, n_tiles, layout);
+    pack_kernel<__half><<<blocks, 256, 0, s>>>((const __half*)w0, (const __half*)w1, k_scale,
+                                               (uint4*)packed, n_out, k, n_tiles, layout);
   if (int rc = check_launch("pack_weights")) return rc;
   // lpc_wsgemm reads the packed weights before waiting on the previous grid:
   // the packed copy must be complete when this call returns
@@ -716,7 +854,7 @@ extern "C" int lpc_pack_weights(const void* w0, const void* w1, void* packed, in
 
 extern "C" int lpc_wsgemm(const void* x, const void* packed_w, void* out, const void* resid,
                           int64_t tokens, int64_t n_out, int k, int epilogue, int dtype,
-                          void* stream) {
+                          float norm_eps, void* stream) {
   using namespace lpc;
   if (tokens <= 0 || tokens > MAX_TOKENS || n_out <= 0 || n_out > (1 << 24) || k <= 0 || k % KB) {
     set_error("wsgemm: need 1..%d tokens, 0 < n_out <= 2^24 and k a multiple of 64 "
@@ -735,10 +873,17 @@ extern "C" int lpc_wsgemm(const void* x, const void* packed_w, void* out, const 
     set_error("wsgemm: null or misaligned pointer");
     return LPC_ERR_INVALID;
   }
+  if (norm_eps < 0.f || norm_eps != norm_eps) {
+    set_error("wsgemm: norm_eps must be 0 (no norm) or positive");
+    return LPC_ERR_INVALID;
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool norm = norm_eps > 0.f;
   if (dtype == LPC_DTYPE_BF16)
-    return launch_epi<__nv_bfloat16>(epilogue, x, packed_w, out, resid, tokens, n_out, k, dtype, s);
-  return launch_epi<__half>(epilogue, x, packed_w, out, resid, tokens, n_out, k, dtype, s);
+    return norm ? launch_epi<__nv_bfloat16, true>(epilogue, x, packed_w, out, resid, tokens, n_out, k, dtype, s, norm_eps)
+                : launch_epi<__nv_bfloat16, false>(epilogue, x, packed_w, out, resid, tokens, n_out, k, dtype, s, 0.f);
+  return norm ? launch_epi<__half, true>(epilogue, x, packed_w, out, resid, tokens, n_out, k, dtype, s, norm_eps)
+              : launch_epi<__half, false>(epilogue, x, packed_w, out, resid, tokens, n_out, k, dtype, s, 0.f);
 }
 
 extern "C" int lpc_qkv_rope_append(const void* x, const void* packed_w, const int64_t* positions,
@@ -747,7 +892,7 @@ extern "C" int lpc_qkv_rope_append(const void* x, const void* packed_w, const in
                                    const int64_t* seq_base, const int32_t* seq_cap, int64_t batch,
                                    int64_t seq, int num_heads, int num_kv_heads, int head_dim, int k,
                                    int64_t max_batch, int64_t max_seq_len, int64_t total_rows,
-                                   int dtype, int table_dtype, void* stream) {
+                                   int dtype, int table_dtype, float norm_eps, void* stream) {
   using namespace lpc;
   const int64_t tokens = batch * seq;
   if (batch <= 0 || seq <= 0 || tokens > MAX_TOKENS || num_heads <= 0 || num_kv_heads <= 0 ||
@@ -791,9 +936,16 @@ extern "C" int lpc_qkv_rope_append(const void* x, const void* packed_w, const in
   qa.total_rows = total_rows;
   qa.H = num_heads;
   qa.Hkv = num_kv_heads;
+  if (norm_eps < 0.f || norm_eps != norm_eps) {
+    set_error("qkv_rope_append: norm_eps must be 0 (no norm) or positive");
+    return LPC_ERR_INVALID;
+  }
   const int64_t n_out = (int64_t)(num_heads + 2 * num_kv_heads) * HEAD_DIM;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool norm = norm_eps > 0.f;
   if (dtype == LPC_DTYPE_BF16)
-    return launch<__nv_bfloat16, EPI_QKV>(x, packed_w, nullptr, nullptr, tokens, n_out, k, dtype, s, qa);
-  return launch<__half, EPI_QKV>(x, packed_w, nullptr, nullptr, tokens, n_out, k, dtype, s, qa);
+    return norm ? launch<__nv_bfloat16, EPI_QKV, true>(x, packed_w, nullptr, nullptr, tokens, n_out, k, dtype, s, norm_eps, qa)
+                : launch<__nv_bfloat16, EPI_QKV, false>(x, packed_w, nullptr, nullptr, tokens, n_out, k, dtype, s, 0.f, qa);
+  return norm ? launch<__half, EPI_QKV, true>(x, packed_w, nullptr, nullptr, tokens, n_out, k, dtype, s, norm_eps, qa)
+              : launch<__half, EPI_QKV, false>(x, packed_w, nullptr, nullptr, tokens, n_out, k, dtype, s, 0.f, qa);
 }

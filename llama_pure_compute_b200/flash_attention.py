@@ -3,9 +3,12 @@
 ``flash_attention_v2(q, k, v, causal=True, sm_scale=None)`` keeps the argument
 checks and error types of src/llama_pure_compute/triton_kernels/
 flash_attention.py:998-1098.  Dispatch:
-  * q_len == 1           -> split-KV decode kernel (lpc_decode_attention);
+  * q_len == 1           -> split-KV decode kernel (lpc_decode_attention),
+    head_dim 32, 64 or 128;
   * otherwise            -> tcgen05 flash-attention kernel (lpc_flash_attention),
-    causal or not, q_len <= kv_len with bottom-right alignment.
+    causal or not, q_len <= kv_len with bottom-right alignment; head_dim 64
+    and 128 natively, head_dim 32 by zero-padding q/k/v to 64 columns (the
+    padded dims add nothing to q.k and give zero output columns, dropped).
 K and V may be sequence slices of a preallocated ``[B, H, S_max, D]`` cache
 (the views ``KVCacheManager.update`` returns): they are read in place through
 their strides, without the reference's ``.contiguous()`` copy of the prefix
@@ -104,6 +107,10 @@ def flash_attention_v2(
         out = decode_attention(q.view(bq, hq, d), kc, vc, lens, sm_scale)
         return out.view(bq, hq, 1, d)
 
+    if d == 32:
+        pad = lambda t: torch.nn.functional.pad(t, (0, 32))  # noqa: E731
+        out = flash_attention_v2(pad(q), pad(k), pad(v), causal=causal, sm_scale=sm_scale)
+        return out[..., :32].contiguous()
     out = torch.empty_like(q)
     rc = _lib.load().lpc_flash_attention(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), bq, hq, hk, q_len, kv_len, d,

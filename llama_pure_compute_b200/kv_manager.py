@@ -243,11 +243,14 @@ class KVCacheManager:
 
     def attend(self, *, layer_idx: int, positions: torch.Tensor, ctx, num_heads: int,
                scale: float, qkv: Optional[torch.Tensor] = None,
-               x: Optional[torch.Tensor] = None, packed_qkv=None) -> torch.Tensor:
-        """RoPE + append of ``qkv`` [B, S, (H+2Hkv)*D] -- or, given the normed
-        hidden states ``x`` and the "heads"-packed q/k/v weight, the projection
-        with RoPE and the append fused in one kernel -- then causal attention
-        of the new queries over the cached context; returns [B, S, H*D]."""
+               x: Optional[torch.Tensor] = None, packed_qkv=None,
+               norm_eps: float = 0.0) -> torch.Tensor:
+        """RoPE + append of ``qkv`` [B, S, (H+2Hkv)*D] -- or, given the hidden
+        states ``x`` and the "heads"-packed q/k/v weight, the projection with
+        RoPE and the append fused in one kernel (``norm_eps > 0``: ``x`` is the
+        raw residual stream and the input RMSNorm, folded into the packed
+        weight, runs in the same kernel) -- then causal attention of the new
+        queries over the cached context; returns [B, S, H*D]."""
         if packed_qkv is not None:
             B, S, _ = x.shape
             self._check_layer(layer_idx)
@@ -255,7 +258,7 @@ class KVCacheManager:
                 raise ValueError("batch size exceeds cache capacity")
             q = qkv_rope_append(x, packed_qkv, positions, ctx.cos_table, ctx.sin_table,
                                 self.k_cache[layer_idx], self.v_cache[layer_idx], num_heads,
-                                self.n_kv_heads)
+                                self.n_kv_heads, norm_eps=norm_eps)
         else:
             B, S, _ = qkv.shape
             q = self.append_qkv(layer_idx=layer_idx, qkv=qkv, positions=positions,

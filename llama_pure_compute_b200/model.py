@@ -9,18 +9,25 @@ checkpoints and call sites carry over.  What runs underneath:
                        (cuBLAS through torch; the q/k/v parameters are views of it)
   RoPE + KV append  -> lpc_rope_kv_append (model.py:146-168 fused into one kernel;
                        per-row positions, so batches may be ragged)
-                       decode steps of <= 32 tokens (head_dim 128): projection,
-                       RoPE and KV append in one kernel, lpc_qkv_rope_append,
-                       on a packed copy of the q/k/v weight
+                       decode steps of <= FUSED_QKV_MAX_TOKENS tokens (head_dim
+                       128): input norm, projection, RoPE and KV append in one
+                       kernel, lpc_qkv_rope_append, on a packed copy of the
+                       q/k/v weight with the norm weight folded in
   attention         -> decode: lpc_decode_attention over device seq_lens
                        (no per-layer .item() sync, model.py:159-161);
                        prefill / no cache: lpc_flash_attention (tcgen05)
-  o_proj + residual -> one addmm (residual added in the GEMM epilogue)
-  post norm + SwiGLU-> lpc_rmsswiglu_forward (model.py:315-321; tcgen05 GEMM
-                       with the SiLU*up epilogue, no torch.cat of weights);
-                       decode steps of <= 128 tokens: lpc_rmsnorm_forward +
-                       lpc_wsgemm on a packed copy of gate/up
-  down + residual   -> one addmm
+  o_proj + residual -> one addmm (residual added in the GEMM epilogue); decode
+                       steps of <= PACKED_RESIDUAL_MAX_TOKENS tokens: lpc_wsgemm
+                       (residual epilogue) on a packed copy of o_proj
+  post norm + SwiGLU-> lpc_rmsswiglu_folded_forward (model.py:315-321): the norm
+                       inside the CTA-pair tcgen05 GEMM with the SiLU*up
+                       epilogue, on gate/up with the norm weight folded in (no
+                       torch.cat of weights, no normalised copy in HBM);
+                       decode steps of <= 128 tokens: the norm and SiLU*up in
+                       one lpc_wsgemm on a packed copy of gate/up (norm weight
+                       folded in)
+  down + residual   -> one addmm; decode steps of <= PACKED_RESIDUAL_MAX_TOKENS
+                       tokens: lpc_wsgemm (residual epilogue), packed down_proj
   lm_head           -> all positions by default (model.py:475), or only the
                        last one with ``last_token_only=True``
 
@@ -45,10 +52,13 @@ from .rmsnorm import RMSNorm
 # Decode steps with at most this many tokens run the SwiGLU GEMM on packed
 # weights (lpc_wsgemm); the packed copy of gate/up is built on first use.
 PACKED_SWIGLU_MAX_TOKENS = 128
-# Decode steps with at most this many tokens run the q/k/v projection with
-# RoPE and the KV append in its epilogue (lpc_qkv_rope_append) on a packed
-# copy of the q/k/v weight, built on first use.
-FUSED_QKV_MAX_TOKENS = 32
+# Decode steps with at most this many tokens run the input norm, the q/k/v
+# projection, RoPE and the KV append in one kernel (lpc_qkv_rope_append) on a
+# packed copy of the q/k/v weight, built on first use.
+FUSED_QKV_MAX_TOKENS = 64
+# Decode steps with at most this many tokens run o_proj and down_proj with the
+# residual add on packed copies of their weights (lpc_wsgemm).
+PACKED_RESIDUAL_MAX_TOKENS = 32
 
 __all__ = ["precompute_freqs_cis", "LlamaAttention", "LlamaDecodeLayer", "LlamaModel",
            "LlamaForCausalLM"]
@@ -80,7 +90,7 @@ class _StepContext:
     """Per-forward data shared by all layers (computed once, not per layer)."""
 
     __slots__ = ("positions", "seq_lens", "start_pos", "cos_table", "sin_table", "decode",
-                 "workspace", "packed_max", "fused_qkv_max")
+                 "workspace", "packed_max", "fused_qkv_max", "resid_max", "fuse_norm")
 
     def __init__(self):
         self.positions = None
@@ -91,7 +101,14 @@ class _StepContext:
         self.decode = False
         self.packed_max = 0
         self.fused_qkv_max = 0
+        self.resid_max = 0
+        self.fuse_norm = True
         self.workspace = None
+
+
+def _packable(x: torch.Tensor, w: torch.Tensor) -> bool:
+    return (x.dtype in (torch.bfloat16, torch.float16) and w.dtype == x.dtype
+            and x.shape[-1] % 64 == 0 and w.is_cuda)
 
 
 class LlamaAttention(nn.Module):
@@ -112,6 +129,8 @@ class LlamaAttention(nn.Module):
         self._qkv = None
         self._packed_qkv = None
         self._packed_qkv_key = None
+        self._packed_o = None
+        self._packed_o_key = None
 
     def qkv_weight(self) -> torch.Tensor:
         """[(H+2Hkv)*D, dim] weight; q/k/v parameters are re-pointed into it once."""
@@ -130,18 +149,28 @@ class LlamaAttention(nn.Module):
             self._qkv_key = tuple(_weight_key(w) for w in ws)
         return self._qkv
 
-    def packed_qkv(self):
+    def packed_qkv(self, norm_weight: Optional[torch.Tensor] = None):
         """The q/k/v weight in the packed "heads" layout (lpc_pack_weights),
-        built on first use and rebuilt when the weight changes."""
+        with ``norm_weight`` (the input RMSNorm's) folded in when given; built
+        on first use and rebuilt when a weight changes."""
         from .packed_linear import PackedWeight
         w = self.qkv_weight()
         # the stacked weight may be an inference tensor (no version counter):
         # key on the q/k/v parameters it was built from
-        key = (w.data_ptr(), self._qkv_key)
+        key = (w.data_ptr(), self._qkv_key, None if norm_weight is None else _weight_key(norm_weight))
         if self._packed_qkv is None or key != self._packed_qkv_key:
-            self._packed_qkv = PackedWeight(w, layout="heads")
+            self._packed_qkv = PackedWeight(w, layout="heads", norm_weight=norm_weight)
             self._packed_qkv_key = key
         return self._packed_qkv
+
+    def packed_o(self):
+        """o_proj in the packed linear layout, built on first use."""
+        from .packed_linear import PackedWeight
+        key = _weight_key(self.o_proj.weight)
+        if self._packed_o is None or key != self._packed_o_key:
+            self._packed_o = PackedWeight(self.o_proj.weight)
+            self._packed_o_key = key
+        return self._packed_o
 
     def _fused_qkv(self, x: torch.Tensor, ctx: Optional[_StepContext]) -> bool:
         return (ctx is not None and ctx.decode and 0 < x.numel() // x.shape[-1] <= ctx.fused_qkv_max
@@ -161,8 +190,13 @@ class LlamaAttention(nn.Module):
         mask: Optional[torch.Tensor] = None,
         use_triton_flash: bool = True,
         ctx: Optional[_StepContext] = None,
+        input_norm: Optional[RMSNorm] = None,
     ) -> torch.Tensor:
-        """Attention block output before the residual add (model.py:110-249)."""
+        """Attention block output before the residual add (model.py:110-249).
+
+        ``input_norm``: ``x`` is the raw residual stream and this RMSNorm is
+        applied inside the fused decode kernel (only on the path where
+        ``fuses_input_norm`` holds)."""
         if mask is not None:
             raise NotImplementedError(
                 "custom attention masks are not supported by the B200 kernels; causal attention "
@@ -170,9 +204,16 @@ class LlamaAttention(nn.Module):
         B, S, _ = x.shape
         H, Hkv, D = self.num_heads, self.num_kv_heads, self.head_dim
         if kv_cache is not None and self._fused_qkv(x, ctx):
-            # decode-sized: projection + RoPE + KV append in one kernel
+            # decode-sized: (input norm +) projection + RoPE + KV append in one kernel
+            if input_norm is not None:
+                return kv_cache.attend(layer_idx=layer_idx, x=x,
+                                       packed_qkv=self.packed_qkv(input_norm.weight),
+                                       norm_eps=input_norm.eps, positions=positions, ctx=ctx,
+                                       num_heads=H, scale=self.scale)
             return kv_cache.attend(layer_idx=layer_idx, x=x, packed_qkv=self.packed_qkv(),
                                    positions=positions, ctx=ctx, num_heads=H, scale=self.scale)
+        if input_norm is not None:
+            raise ValueError("input_norm is only applied inside the fused decode kernel")
         qkv = F.linear(x, self.qkv_weight())
         if kv_cache is not None:
             if ctx is None or ctx.cos_table is None:
@@ -191,11 +232,23 @@ class LlamaAttention(nn.Module):
             out = out.transpose(1, 2).reshape(B, S, H * D)
         return out
 
-    def project_out(self, attn: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
-        """residual + attn @ o_proj^T in one GEMM (beta=1 epilogue)."""
+    def fuses_input_norm(self, x: torch.Tensor, ctx: Optional[_StepContext]) -> bool:
+        """Whether this step's input norm runs inside the q/k/v kernel."""
+        return self._fused_qkv(x, ctx)
+
+    def project_out(self, attn: torch.Tensor, residual: torch.Tensor,
+                    ctx: Optional[_StepContext] = None) -> torch.Tensor:
+        """residual + attn @ o_proj^T in one GEMM (the residual added in the
+        epilogue): the packed weight-streaming kernel for decode steps of at
+        most ``ctx.resid_max`` tokens, else cuBLAS (beta=1 epilogue)."""
         shp = residual.shape
         r2 = residual.reshape(-1, shp[-1])
-        return torch.addmm(r2, attn.reshape(-1, attn.shape[-1]), self.o_proj.weight.t()).view(shp)
+        a2 = attn.reshape(-1, attn.shape[-1])
+        if (ctx is not None and ctx.decode and a2.shape[0] <= ctx.resid_max
+                and _packable(a2, self.o_proj.weight) and r2.is_contiguous()):
+            from .packed_linear import packed_linear
+            return packed_linear(a2, self.packed_o(), "residual", resid=r2).view(shp)
+        return torch.addmm(r2, a2, self.o_proj.weight.t()).view(shp)
 
 
 class LlamaDecodeLayer(nn.Module):
@@ -210,33 +263,85 @@ class LlamaDecodeLayer(nn.Module):
         self.down_proj = nn.Linear(config.inter_dim, config.dim, bias=False)
         self._packed_gate_up = None
         self._packed_key = None
+        self._packed_down = None
+        self._packed_down_key = None
+        self._folded = None
+        self._folded_key = None
 
     def packed_gate_up(self):
-        """gate/up weights in the packed SwiGLU tile layout (lpc_pack_weights),
-        built on first use and rebuilt when either weight changes."""
+        """gate/up weights in the packed SwiGLU tile layout (lpc_pack_weights)
+        with the post-attention norm weight folded in; built on first use and
+        rebuilt when a weight changes."""
         from .packed_linear import PackedWeight
-        ws = (self.gate_proj.weight, self.up_proj.weight)
+        nw = self.post_attention_layernorm.weight
+        ws = (self.gate_proj.weight, self.up_proj.weight, nw)
         key = tuple(_weight_key(w) for w in ws)
         if self._packed_gate_up is None or key != self._packed_key:
-            self._packed_gate_up = PackedWeight(ws[0], ws[1], layout="swiglu")
+            self._packed_gate_up = PackedWeight(ws[0], ws[1], layout="swiglu", norm_weight=nw)
             self._packed_key = key
         return self._packed_gate_up
 
-    def _mlp_inter(self, h: torch.Tensor, packed_max: int) -> torch.Tensor:
+    def packed_down(self):
+        """down_proj in the packed linear layout, built on first use."""
+        from .packed_linear import PackedWeight
+        key = _weight_key(self.down_proj.weight)
+        if self._packed_down is None or key != self._packed_down_key:
+            self._packed_down = PackedWeight(self.down_proj.weight)
+            self._packed_down_key = key
+        return self._packed_down
+
+    def folded_gate_up(self):
+        """(gate, up) weights with the post-attention norm weight folded in
+        (W[n, k] * w[k]) for the one-kernel norm + SwiGLU; the parameters
+        themselves when w is all ones.  Built outside stream capture (it reads
+        w on the host once per weight version); None while capturing."""
+        nw = self.post_attention_layernorm.weight
+        ws = (self.gate_proj.weight, self.up_proj.weight, nw)
+        key = tuple(_weight_key(w) for w in ws)
+        if self._folded is None or key != self._folded_key:
+            if torch.cuda.is_current_stream_capturing():
+                return None
+            with torch.no_grad():
+                if bool((nw == 1).all()):
+                    self._folded = (ws[0], ws[1])
+                else:
+                    scale = nw.float().unsqueeze(0)
+                    self._folded = tuple((w.float() * scale).to(w.dtype) for w in ws[:2])
+                    # the GEMM streams weights before it waits on earlier kernels
+                    torch.cuda.current_stream(nw.device).synchronize()
+            self._folded_key = key
+        return self._folded
+
+    def _mlp_inter(self, h: torch.Tensor, packed_max: int, fuse_norm: bool = True) -> torch.Tensor:
         norm = self.post_attention_layernorm
         tokens = h.numel() // h.shape[-1]
-        w = self.gate_proj.weight
-        if (tokens <= packed_max and h.dtype in (torch.bfloat16, torch.float16)
-                and w.dtype == h.dtype and h.shape[-1] % 64 == 0):
-            # decode-sized: norm, then the weight-streaming GEMM on packed
-            # weights with the SiLU*up epilogue (faster than the activation-
-            # major tile of the fused op at these token counts)
-            from .ops import rmsnorm_forward
+        if tokens <= packed_max and _packable(h, self.gate_proj.weight):
+            # decode-sized: the norm and SiLU*up in one weight-streaming GEMM
+            # on the packed gate/up (norm weight folded in; each token's
+            # rsqrt(mean(h^2) + eps) taken inside the kernel)
             from .packed_linear import packed_linear
-            normed = rmsnorm_forward(h, norm.weight, norm.eps)
-            return packed_linear(normed, self.packed_gate_up(), "swiglu")
+            return packed_linear(h, self.packed_gate_up(), "swiglu", norm_eps=norm.eps)
+        if (fuse_norm and _packable(h, self.gate_proj.weight)
+                and self.gate_proj.weight.shape[0] % 16 == 0):
+            folded = self.folded_gate_up()
+            if folded is not None:
+                # the norm inside the CTA-pair SwiGLU GEMM (statistics from its
+                # activation tiles, the row scale in the epilogue)
+                from .ops import rmsswiglu_folded_forward
+                return rmsswiglu_folded_forward(h, folded[0], folded[1], norm.eps)
         return rmsswiglu_forward(h, rms_weight=norm.weight, gate_w=self.gate_proj.weight,
                                  up_w=self.up_proj.weight, eps=norm.eps)
+
+    def _down(self, inter: torch.Tensor, h: torch.Tensor, ctx: Optional[_StepContext]) -> torch.Tensor:
+        """h + inter @ down_proj^T (residual in the GEMM epilogue)."""
+        shp = h.shape
+        h2 = h.reshape(-1, shp[-1])
+        i2 = inter.reshape(-1, inter.shape[-1])
+        if (ctx is not None and ctx.decode and i2.shape[0] <= ctx.resid_max
+                and _packable(i2, self.down_proj.weight) and h2.is_contiguous()):
+            from .packed_linear import packed_linear
+            return packed_linear(i2, self.packed_down(), "residual", resid=h2).view(shp)
+        return torch.addmm(h2, i2, self.down_proj.weight.t()).view(shp)
 
     def forward(
         self,
@@ -249,13 +354,18 @@ class LlamaDecodeLayer(nn.Module):
         mask: Optional[torch.Tensor],
         ctx: Optional[_StepContext] = None,
     ) -> torch.Tensor:
-        attn = self.self_attn(self.input_layernorm(x), positions=positions, cos=cos, sin=sin,
-                              kv_cache=kv_cache, layer_idx=self.layer_idx, mask=mask, ctx=ctx)
-        h = self.self_attn.project_out(attn, x)
-        mlp_inter = self._mlp_inter(h, ctx.packed_max if ctx is not None and ctx.decode else 0)
-        shp = h.shape
-        return torch.addmm(h.reshape(-1, shp[-1]), mlp_inter.reshape(-1, mlp_inter.shape[-1]),
-                           self.down_proj.weight.t()).view(shp)
+        if kv_cache is not None and self.self_attn.fuses_input_norm(x, ctx):
+            # the input norm runs inside the fused q/k/v kernel
+            attn = self.self_attn(x, positions=positions, cos=cos, sin=sin, kv_cache=kv_cache,
+                                  layer_idx=self.layer_idx, mask=mask, ctx=ctx,
+                                  input_norm=self.input_layernorm)
+        else:
+            attn = self.self_attn(self.input_layernorm(x), positions=positions, cos=cos, sin=sin,
+                                  kv_cache=kv_cache, layer_idx=self.layer_idx, mask=mask, ctx=ctx)
+        h = self.self_attn.project_out(attn, x, ctx)
+        mlp_inter = self._mlp_inter(h, ctx.packed_max if ctx is not None and ctx.decode else 0,
+                                    ctx.fuse_norm if ctx is not None else True)
+        return self._down(mlp_inter, h, ctx)
 
 
 class LlamaModel(nn.Module):
@@ -271,9 +381,16 @@ class LlamaModel(nn.Module):
         # decode steps with at most this many tokens use the packed SwiGLU
         # weights (0 disables the packed copy, e.g. when HBM is tight)
         self.packed_swiglu_max_tokens = PACKED_SWIGLU_MAX_TOKENS
-        # decode steps with at most this many tokens use the fused q/k/v
-        # projection + RoPE + KV append on a packed q/k/v copy (0 disables it)
+        # decode steps with at most this many tokens use the fused input norm +
+        # q/k/v projection + RoPE + KV append on a packed q/k/v copy (0 disables it)
         self.fused_qkv_max_tokens = FUSED_QKV_MAX_TOKENS
+        # decode steps with at most this many tokens run o_proj / down_proj
+        # with the residual on packed copies (0 disables them)
+        self.packed_residual_max_tokens = PACKED_RESIDUAL_MAX_TOKENS
+        # larger steps run the post-attention norm inside the SwiGLU GEMM on
+        # gate/up weights with the norm weight folded in (a folded copy is made
+        # only when that weight is not all ones); False: separate norm kernel
+        self.fuse_mlp_norm = True
 
     def reset_rope_tables(self) -> None:
         """Recompute cos/sin (e.g. after materialising a meta-device model)."""
@@ -298,6 +415,8 @@ class LlamaModel(nn.Module):
         ctx.positions = positions
         ctx.packed_max = self.packed_swiglu_max_tokens
         ctx.fused_qkv_max = self.fused_qkv_max_tokens
+        ctx.resid_max = self.packed_residual_max_tokens
+        ctx.fuse_norm = self.fuse_mlp_norm
         cos = sin = None
         if kv_cache is not None:
             ctx.cos_table, ctx.sin_table = self.cos_cached, self.sin_cached

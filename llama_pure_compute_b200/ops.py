@@ -200,6 +200,40 @@ def rmsswiglu_forward(
     return out
 
 
+def rmsswiglu_folded_forward(x: torch.Tensor, gate_w: torch.Tensor, up_w: Optional[torch.Tensor],
+                             eps: float = 1e-5) -> torch.Tensor:
+    """``silu(norm(x) Wg^T) * (norm(x) Wu^T)`` in one kernel, for weights that
+    already carry the norm weight (``gate_w = Wg * rms_weight`` column-wise,
+    e.g. folded once when a model is loaded; ``up_w`` None: ``gate_w`` is the
+    fused ``[2I, D]`` form).  The tcgen05 CTA-pair GEMM reads the raw rows of
+    ``x``, takes each row's sum of squares from the tiles it feeds the tensor
+    core and scales the accumulators by ``rsqrt(mean(x^2) + eps)``: the norm of
+    ops.py:45-59 without its HBM round trip (rmsswiglu.cu:176-196)."""
+    for t, n in ((x, "x"), (gate_w, "gate_w")):
+        _require_cuda(t, n)
+    if eps <= 0.0:
+        raise ValueError("LlamaPureComputeError: eps must be strictly positive.")
+    x = x.contiguous()
+    gate_w = gate_w.contiguous()
+    D = x.shape[-1]
+    fused = up_w is None
+    inter = gate_w.shape[0] // 2 if fused else gate_w.shape[0]
+    if gate_w.dim() != 2 or gate_w.shape[1] != D or (up_w is not None and tuple(up_w.shape) != (inter, D)):
+        raise ValueError("LlamaPureComputeError: gate_w/up_w must be [inter, dim].")
+    if gate_w.dtype != x.dtype or (up_w is not None and up_w.dtype != x.dtype):
+        raise TypeError("LlamaPureComputeError: gate_w/up_w must have x's dtype.")
+    up_c = None if up_w is None else up_w.contiguous()
+    tokens = x.numel() // D
+    out = torch.empty(*x.shape[:-1], inter, dtype=x.dtype, device=x.device)
+    rc = _lib.load().lpc_rmsswiglu_folded_forward(
+        x.data_ptr(), gate_w.data_ptr(), _lib.ptr(up_c), out.data_ptr(), tokens, D, inter,
+        float(eps), _lib.dtype_code(x.dtype, "rmsswiglu_folded_forward"), _lib.stream_of(x))
+    _lib.check(rc, "rmsswiglu_folded_forward")
+    if tokens:
+        _lib.count_launch("lpc_rmsswiglu_folded_forward")
+    return out
+
+
 # ---------------------------------------------------------------------------
 # KV cache
 # ---------------------------------------------------------------------------
@@ -411,9 +445,14 @@ def qkv_rope_append(
     seq_base: Optional[torch.Tensor] = None,
     seq_cap: Optional[torch.Tensor] = None,
     q_out: Optional[torch.Tensor] = None,
+    norm_eps: float = 0.0,
 ) -> torch.Tensor:
     """The attention block's q/k/v projection with RoPE and the KV append in
     its epilogue (model.py:125-168 + kv_manager.py:260-300 in one kernel).
+
+    ``norm_eps > 0``: ``x`` are the raw hidden states and the input RMSNorm
+    (model.py:305) runs inside the kernel; ``packed_qkv`` must then be packed
+    with that norm's weight (``PackedWeight(..., norm_weight=w)``).
 
     ``x`` [B, S, dim] are the normed hidden states, ``packed_qkv`` the stacked
     q/k/v weight packed with layout "heads" (head_dim 128), B * S <= 256.
@@ -447,6 +486,9 @@ def qkv_rope_append(
         raise ValueError("LlamaPureComputeError: packed weight does not match heads * head_dim.")
     if dim != packed_qkv.k or x.dtype != packed_qkv.dtype:
         raise ValueError("LlamaPureComputeError: x must be [..., k] in the weight's dtype.")
+    if norm_eps < 0 or (norm_eps > 0) != getattr(packed_qkv, "folds_norm", False):
+        raise ValueError("LlamaPureComputeError: norm_eps > 0 needs a weight packed with its "
+                         "norm_weight (and only such a weight).")
     if cos_table.shape[-1] != D or cos_table.dim() != 2:
         raise ValueError("LlamaPureComputeError: rope tables must be [max_pos, head_dim].")
     x = x.contiguous()
@@ -460,7 +502,7 @@ def qkv_rope_append(
         sin_table.data_ptr(), cos_table.shape[0], q_out.data_ptr(), key_cache.data_ptr(),
         value_cache.data_ptr(), _lib.ptr(seq_base), _lib.ptr(seq_cap), B, S, num_heads,
         num_kv_heads, D, dim, Bmax, Smax, total_rows, _lib.dtype_code(x.dtype, "qkv_rope_append"),
-        _lib.dtype_code(cos_table.dtype, "qkv_rope_append"), _lib.stream_of(x))
+        _lib.dtype_code(cos_table.dtype, "qkv_rope_append"), float(norm_eps), _lib.stream_of(x))
     _lib.check(rc, "qkv_rope_append")
     _lib.count_launch("lpc_qkv_rope_append")
     return q_out

@@ -38,10 +38,16 @@ class PackedWeight:
     weight (ops.py:118-131 accepts both forms).
     layout "heads": ``w0`` is the stacked q/k/v projection weight
     ``[(H + 2 Hkv) * 128, k]`` (head_dim 128), for ``ops.qkv_rope_append``.
+
+    ``norm_weight`` (``[k]``, optional) is the weight of the RMSNorm whose
+    output this projection consumes.  It is folded into the packed copy
+    (``W[n, k] * norm_weight[k]``, one rounding), so that the product can
+    normalise its raw input rows itself: ``packed_linear(..., norm_eps=eps)``
+    / ``qkv_rope_append(..., norm_eps=eps)``.  ``folds_norm`` records it.
     """
 
     def __init__(self, w0: torch.Tensor, w1: Optional[torch.Tensor] = None,
-                 layout: str = "linear"):
+                 layout: str = "linear", norm_weight: Optional[torch.Tensor] = None):
         if layout not in LAYOUTS:
             raise ValueError(f"LlamaPureComputeError: unknown packed layout {layout!r}")
         if not w0.is_cuda:
@@ -63,6 +69,13 @@ class PackedWeight:
                 raise ValueError("LlamaPureComputeError: up weight must match the gate weight.")
         self.n_out, self.k, self.layout, self.dtype = n_out, k, layout, w0.dtype
         self.device = w0.device
+        scale = None
+        if norm_weight is not None:
+            if norm_weight.numel() != k or norm_weight.device != w0.device:
+                raise ValueError("LlamaPureComputeError: norm_weight must be [k] on the weight's "
+                                 "device.")
+            scale = norm_weight.detach().reshape(-1).to(torch.float32).contiguous()
+        self.folds_norm = scale is not None
         lib = _lib.load()
         code = _lib.dtype_code(w0.dtype, "pack_weights")
         nbytes = lib.lpc_packed_weight_bytes(n_out, k, lay)
@@ -72,8 +85,9 @@ class PackedWeight:
                              "multiple of 128).")
         with torch.cuda.device(w0.device):
             self.data = torch.empty(nbytes, dtype=torch.uint8, device=w0.device)
-            rc = lib.lpc_pack_weights(w0.data_ptr(), _lib.ptr(w1), self.data.data_ptr(), n_out, k,
-                                      lay, code, _lib.stream_of(w0))
+            rc = lib.lpc_pack_weights(w0.data_ptr(), _lib.ptr(w1), _lib.ptr(scale),
+                                      self.data.data_ptr(), n_out, k, lay, code,
+                                      _lib.stream_of(w0))
         _lib.check(rc, "pack_weights")
         _lib.count_launch("lpc_pack_weights")
 
@@ -85,12 +99,18 @@ class PackedWeight:
 
 def packed_linear(x: torch.Tensor, w: PackedWeight, epilogue: str = "store",
                   resid: Optional[torch.Tensor] = None,
-                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                  out: Optional[torch.Tensor] = None, norm_eps: float = 0.0) -> torch.Tensor:
     """``epilogue(x w^T)`` for ``x [..., k]`` with at most 256 rows.
 
     "store": x w^T.  "residual": resid + x w^T (``out`` may be ``resid``).
     "swiglu": silu(x Wg^T) * (x Wu^T) on a weight packed with layout "swiglu".
     fp32 accumulation, one rounding to x's dtype.
+
+    ``norm_eps > 0`` (a weight packed with ``norm_weight``): ``x`` are the raw
+    rows of an RMSNorm and the product is that of the normalised rows, i.e.
+    ``epilogue(rmsnorm(x) W^T)``, computed without writing them: each token's
+    accumulators are scaled by rsqrt(mean(x^2) + eps), its sum of squares taken
+    from the activation tiles inside the kernel.
     """
     if epilogue not in EPILOGUES:
         raise ValueError(f"LlamaPureComputeError: unknown epilogue {epilogue!r}")
@@ -98,6 +118,9 @@ def packed_linear(x: torch.Tensor, w: PackedWeight, epilogue: str = "store",
         raise ValueError("LlamaPureComputeError: the swiglu epilogue needs a swiglu-packed weight.")
     if w.layout == "heads":
         raise ValueError("LlamaPureComputeError: a 'heads'-packed weight is for qkv_rope_append.")
+    if norm_eps < 0 or (norm_eps > 0) != w.folds_norm:
+        raise ValueError("LlamaPureComputeError: norm_eps > 0 needs a weight packed with its "
+                         "norm_weight (and only such a weight).")
     if not x.is_cuda:
         raise ValueError("LlamaPureComputeError: x must be on CUDA device.")
     if x.shape[-1] != w.k or x.dtype != w.dtype:
@@ -123,7 +146,7 @@ def packed_linear(x: torch.Tensor, w: PackedWeight, epilogue: str = "store",
         raise ValueError("LlamaPureComputeError: out must be a contiguous [..., n_out] tensor.")
     rc = _lib.load().lpc_wsgemm(x2.data_ptr(), w.data.data_ptr(), out.data_ptr(), rp, tokens,
                                 w.n_out, w.k, epi, _lib.dtype_code(x.dtype, "packed_linear"),
-                                _lib.stream_of(x))
+                                float(norm_eps), _lib.stream_of(x))
     _lib.check(rc, "packed_linear")
     _lib.count_launch("lpc_wsgemm")
     return out

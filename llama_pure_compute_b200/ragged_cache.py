@@ -117,14 +117,15 @@ class RaggedKVCache:
 
     def attend(self, *, layer_idx: int, positions: torch.Tensor, ctx, num_heads: int,
                scale: float, qkv: Optional[torch.Tensor] = None,
-               x: Optional[torch.Tensor] = None, packed_qkv=None) -> torch.Tensor:
+               x: Optional[torch.Tensor] = None, packed_qkv=None,
+               norm_eps: float = 0.0) -> torch.Tensor:
         D = self.head_dim
         kc, vc = self.k_cache[layer_idx], self.v_cache[layer_idx]
         if packed_qkv is not None:
             B, S, _ = x.shape
             q = qkv_rope_append(x, packed_qkv, positions, ctx.cos_table, ctx.sin_table, kc, vc,
                                 num_heads, self.n_kv_heads, seq_base=self.active_base,
-                                seq_cap=self.active_cap)
+                                seq_cap=self.active_cap, norm_eps=norm_eps)
         else:
             B, S, _ = qkv.shape
             q = rope_kv_append_ragged(qkv, positions, ctx.cos_table, ctx.sin_table, kc, vc,

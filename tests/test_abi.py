@@ -57,23 +57,23 @@ def test_host_validation_without_gpu():
     assert lib.lpc_packed_weight_bytes(300, 100, 0) == 0          # k not a multiple of 64
     assert lib.lpc_packed_weight_bytes(200, 128, 2) == 0          # heads layout: whole heads only
     assert lib.lpc_packed_weight_bytes(256, 128, 2) == 2 * 2 * 16384
-    assert lib.lpc_pack_weights(None, None, None, 128, 64, 3, 2, None) == _lib.LPC_ERR_INVALID
-    assert lib.lpc_wsgemm(None, None, None, None, 257, 128, 64, 0, 2, None) == _lib.LPC_ERR_INVALID
-    assert lib.lpc_wsgemm(None, None, None, None, 8, 128, 64, 1, 2, None) == _lib.LPC_ERR_INVALID
+    assert lib.lpc_pack_weights(None, None, None, None, 128, 64, 3, 2, None) == _lib.LPC_ERR_INVALID
+    assert lib.lpc_wsgemm(None, None, None, None, 257, 128, 64, 0, 2, 0.0, None) == _lib.LPC_ERR_INVALID
+    assert lib.lpc_wsgemm(None, None, None, None, 8, 128, 64, 1, 2, 0.0, None) == _lib.LPC_ERR_INVALID
     assert b"residual needs resid" in lib.lpc_last_error()
     qkv = lib.lpc_qkv_rope_append
     # head_dim other than 128
     assert qkv(None, None, None, None, None, 64, None, None, None, None, None, 2, 1, 4, 4, 64, 256,
-               2, 64, 0, 2, 2, None) == _lib.LPC_ERR_UNSUPPORTED
+               2, 64, 0, 2, 2, 0.0, None) == _lib.LPC_ERR_UNSUPPORTED
     # cos/sin tables in another dtype than the data
     assert qkv(None, None, None, None, None, 64, None, None, None, None, None, 2, 1, 4, 4, 128, 256,
-               2, 64, 0, 2, 0, None) == _lib.LPC_ERR_UNSUPPORTED
+               2, 64, 0, 2, 0, 0.0, None) == _lib.LPC_ERR_UNSUPPORTED
     # more than 256 tokens
     assert qkv(None, None, None, None, None, 64, None, None, None, None, None, 300, 1, 4, 4, 128, 256,
-               300, 64, 0, 2, 2, None) == _lib.LPC_ERR_INVALID
+               300, 64, 0, 2, 2, 0.0, None) == _lib.LPC_ERR_INVALID
     # dense cache smaller than the batch
     assert qkv(None, None, None, None, None, 64, None, None, None, None, None, 4, 1, 4, 4, 128, 256,
-               2, 64, 0, 2, 2, None) == _lib.LPC_ERR_INVALID
+               2, 64, 0, 2, 2, 0.0, None) == _lib.LPC_ERR_INVALID
     assert b"max_batch" in lib.lpc_last_error()
     # zero-sized work is a no-op
     assert lib.lpc_update_kv_cache(None, None, None, None, None, 0, 64, 1, 64, 1, 8, 2, None) == 0
