@@ -45,6 +45,7 @@
 // across items: q_empty (all S MMAs of an item done with Q) releases the Q
 // buffer for the next item, o_free (epilogue has read O_t) gates its first PV_t.
 #include <atomic>
+#include <cstdlib>
 
 #include "lpc_common.cuh"
 
@@ -144,9 +145,14 @@ struct Params {
   int num_items;                  // num_q_blocks * heads * batch
   float scale_log2;
   int causal;
+  int band;                       // (head, batch) pairs per band of the item order
 };
 
-// Work item `i` in longest-first order: query block (descending), head, batch.
+// Work item `i`: the (head, batch) pairs are cut into bands of p.band pairs;
+// within a band, items go longest first: query block (descending), then the
+// band's pairs.  One band spanning every pair is plain longest-first order;
+// narrower bands keep all query blocks of a head in flight together, so the
+// head's K/V tiles are shared through L2 instead of re-read from HBM.
 struct Item {
   int qb, h, b;
   int64_t q0;
@@ -156,8 +162,14 @@ struct Item {
 __device__ __forceinline__ Item decode_item(const Params& p, int i) {
   Item it;
   const int hb = p.heads * p.batch;
-  it.qb = p.num_q_blocks - 1 - i / hb;
-  const int r = i - (i / hb) * hb;
+  const int bw = p.band;
+  const int per_band = bw * p.num_q_blocks;
+  const int band = i / per_band;
+  const int first = band * bw;
+  const int nb = min(bw, hb - first);  // pairs in this band
+  const int within = i - band * per_band;
+  it.qb = p.num_q_blocks - 1 - within / nb;
+  const int r = first + within % nb;
   it.h = r % p.heads;
   it.b = r / p.heads;
   it.q0 = (int64_t)it.qb * (NQT * BQ);
@@ -673,6 +685,14 @@ extern "C" int lpc_flash_attention(const void* q, const void* k, const void* v, 
   p.num_items = (int)items;
   p.scale_log2 = sm_scale * LOG2E;
   p.causal = causal ? 1 : 0;
+  // item order: LPC_PREFILL_BAND=<pairs> narrows the bands (measurement);
+  // by default one band covers every (head, batch) pair
+  {
+    const int hb = heads * (int)batch;
+    const char* e = getenv("LPC_PREFILL_BAND");
+    const int want = e ? atoi(e) : 0;
+    p.band = want > 0 && want < hb ? want : hb;
+  }
   const uint32_t fmt = dtype == LPC_DTYPE_BF16 ? 1u : 0u;
   const uint32_t id_qk = idesc_f16(fmt, BQ, BKV, 0u, 0u);
   const uint32_t id_pv = idesc_f16(fmt, BQ, (uint32_t)head_dim, 0u, 1u);

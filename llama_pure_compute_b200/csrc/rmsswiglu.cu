@@ -429,10 +429,8 @@ __global__ void __launch_bounds__(192)
       float ss = 0.f;
       for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % STAGES;
-        // one lane per warp waits; the warp follows it
-        bool got = true;
-        if (lane == 0) got = lpc::mbar_wait(consumed_bar(s), (uint32_t)(kb / STAGES) & 1u, st);
-        if (!__shfl_sync(0xffffffffu, got, 0)) {
+        // every lane waits: a converged warp sleeps in the wait
+        if (!__all_sync(0xffffffffu, lpc::mbar_wait(consumed_bar(s), (uint32_t)(kb / STAGES) & 1u, st))) {
           stats_ok = false;
           break;
         }

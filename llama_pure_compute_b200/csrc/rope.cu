@@ -13,8 +13,6 @@
 //
 // Each thread owns VEC consecutive rotation pairs of one (token, head): it
 // loads the VEC lower-half and VEC upper-half elements as 16-byte vectors.
-#include <algorithm>
-
 #include "lpc_common.cuh"
 
 LPC_DECLARE_STATUS(g_rope_status)
@@ -153,31 +151,23 @@ __global__ void __launch_bounds__(256) rope_kernel(T* q, T* k, const TT* __restr
 
 // Fused prologue: qkv [B, S, (H + 2Hkv) * D] -> q_out [B, H, S, D] (rotated),
 // key_cache[b, h, pos] (rotated), value_cache[b, h, pos] (copied).
-//
-// A thread owns VEC rotation pairs (chunk c) of one token for a group of
-// `head_group` consecutive heads of the stacked q | k | v row: the token's
-// position, cache row and cos/sin entries are read once per group, and the
-// heads' loads are issued HU at a time before any store.  The host sizes the
-// group so that the grid still holds enough threads to cover the GPU (one
-// head per thread for decode-sized steps, tens of heads for prefill).
-template <typename T, typename TT, int VEC, int HU>  // HU: heads whose loads are in flight together
+template <typename T, typename TT, int VEC>
 __global__ void __launch_bounds__(256) rope_kv_append_kernel(
     const T* __restrict__ qkv, const int64_t* __restrict__ positions, const TT* __restrict__ cosb,
     const TT* __restrict__ sinb, int64_t table_rows, T* __restrict__ q_out,
     T* __restrict__ kcache, T* __restrict__ vcache, int64_t batch, int64_t seq, int num_heads,
     int num_kv_heads, int head_dim, int64_t max_batch, int64_t max_seq_len,
-    const int64_t* __restrict__ seq_base, const int32_t* __restrict__ seq_cap, int64_t total_rows,
-    int head_group, int num_groups) {
+    const int64_t* __restrict__ seq_base, const int32_t* __restrict__ seq_cap, int64_t total_rows) {
   const int half = head_dim >> 1;
   const int chunks = half / VEC;
   const int heads_all = num_heads + 2 * num_kv_heads;
   const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t work = batch * seq * num_groups * chunks;
+  const int64_t work = batch * seq * heads_all * chunks;
   if (gid >= work) return;
   const int c = (int)(gid % chunks);
-  const int64_t tg = gid / chunks;
-  const int grp = (int)(tg % num_groups);
-  const int64_t tok = tg / num_groups;  // b * seq + s
+  const int64_t th = gid / chunks;
+  const int hh = (int)(th % heads_all);
+  const int64_t tok = th / heads_all;  // b * seq + s
   const int64_t b = tok / seq;
   const int64_t s = tok - b * seq;
   const int64_t pos = __ldg(positions + tok);
@@ -199,52 +189,40 @@ __global__ void __launch_bounds__(256) rope_kv_append_kernel(
     head_rows = total_rows;
   }
   if (!ok || pos >= table_rows) {
-    if (grp == 0 && c == 0) atomicOr(&g_rope_status, LPC_DEV_ERR_BOUNDS);
+    atomicOr(&g_rope_status, LPC_DEV_ERR_BOUNDS);
     return;
   }
   const int d = c * VEC;
-  const int h_begin = grp * head_group;
-  const int h_end = min(heads_all, h_begin + head_group);
+  const T* src = qkv + tok * (int64_t)heads_all * head_dim + (int64_t)hh * head_dim;
+  float x0[VEC], x1[VEC];
+  load_f<T, VEC>(src + d, x0);
+  load_f<T, VEC>(src + d + half, x1);
+
+  if (hh >= num_heads + num_kv_heads) {  // V: plain copy into the cache
+    const int h = hh - num_heads - num_kv_heads;
+    T* dst = vcache + (row + h * head_rows) * (int64_t)head_dim;
+    store_f<T, VEC>(dst + d, x0);
+    store_f<T, VEC>(dst + d + half, x1);
+    return;
+  }
   float c0[VEC], s0[VEC], c1[VEC], s1[VEC];
-  if (h_begin < num_heads + num_kv_heads) {  // the group has rotated (q or k) heads
-    const TT* cr = cosb + pos * (int64_t)head_dim;
-    const TT* sr = sinb + pos * (int64_t)head_dim;
-    load_f<TT, VEC>(cr + d, c0);
-    load_f<TT, VEC>(sr + d, s0);
-    load_f<TT, VEC>(cr + d + half, c1);
-    load_f<TT, VEC>(sr + d + half, s1);
+  const TT* cr = cosb + pos * (int64_t)head_dim;
+  const TT* sr = sinb + pos * (int64_t)head_dim;
+  load_f<TT, VEC>(cr + d, c0);
+  load_f<TT, VEC>(sr + d, s0);
+  load_f<TT, VEC>(cr + d + half, c1);
+  load_f<TT, VEC>(sr + d + half, s1);
+  float o0[VEC], o1[VEC];
+  rotate<VEC>(x0, x1, c0, s0, c1, s1, o0, o1);
+  T* dst;
+  if (hh < num_heads) {
+    dst = q_out + ((b * num_heads + hh) * seq + s) * (int64_t)head_dim;
+  } else {
+    const int h = hh - num_heads;
+    dst = kcache + (row + h * head_rows) * (int64_t)head_dim;
   }
-  const T* src_tok = qkv + tok * (int64_t)heads_all * head_dim + d;
-  for (int h0 = h_begin; h0 < h_end; h0 += HU) {
-    float x0[HU][VEC], x1[HU][VEC];
-#pragma unroll
-    for (int u = 0; u < HU; ++u) {
-      if (h0 + u < h_end) {
-        load_f<T, VEC>(src_tok + (int64_t)(h0 + u) * head_dim, x0[u]);
-        load_f<T, VEC>(src_tok + (int64_t)(h0 + u) * head_dim + half, x1[u]);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < HU; ++u) {
-      const int hh = h0 + u;
-      if (hh >= h_end) break;
-      T* dst;
-      if (hh >= num_heads + num_kv_heads) {  // V: plain copy into the cache
-        dst = vcache + (row + (int64_t)(hh - num_heads - num_kv_heads) * head_rows) * head_dim;
-        store_f<T, VEC>(dst + d, x0[u]);
-        store_f<T, VEC>(dst + d + half, x1[u]);
-        continue;
-      }
-      float o0[VEC], o1[VEC];
-      rotate<VEC>(x0[u], x1[u], c0, s0, c1, s1, o0, o1);
-      if (hh < num_heads)
-        dst = q_out + ((b * num_heads + hh) * seq + s) * (int64_t)head_dim;
-      else
-        dst = kcache + (row + (int64_t)(hh - num_heads) * head_rows) * head_dim;
-      store_f<T, VEC>(dst + d, o0);
-      store_f<T, VEC>(dst + d + half, o1);
-    }
-  }
+  store_f<T, VEC>(dst + d, o0);
+  store_f<T, VEC>(dst + d + half, o1);
 }
 
 template <typename T, typename TT>
@@ -288,24 +266,10 @@ int launch_fused(const void* qkv, const int64_t* positions, const void* c, const
                  const int32_t* seq_cap, int64_t total_rows, cudaStream_t s) {
   constexpr int VEC = 16 / (int)sizeof(T);
   const int threads = 256;
-  const int heads_all = h + 2 * hkv;
-  // heads per thread: one while tokens x heads x chunks fill the GPU (about
-  // four waves of 256-thread blocks), more for prefill-sized steps
-  const int64_t per_head = batch * seq * (d / 2 / VEC);
-  const int64_t target = (int64_t)lpc::current_device_sms() * 4 * threads;
-  const int64_t want = (per_head * heads_all + target - 1) / target;
-  const int head_group = (int)std::max<int64_t>(1, std::min<int64_t>(heads_all, want));
-  const int groups = (heads_all + head_group - 1) / head_group;
-  const int64_t work = per_head * groups;
-  const unsigned blocks = (unsigned)((work + threads - 1) / threads);
-  if (head_group == 1)  // one head per thread: few registers, many resident threads
-    rope_kv_append_kernel<T, TT, VEC, 1><<<blocks, threads, 0, s>>>(
-        (const T*)qkv, positions, (const TT*)c, (const TT*)sn, rows, (T*)q_out, (T*)kc, (T*)vc,
-        batch, seq, h, hkv, d, max_batch, max_seq, seq_base, seq_cap, total_rows, head_group, groups);
-  else
-    rope_kv_append_kernel<T, TT, VEC, 4><<<blocks, threads, 0, s>>>(
-        (const T*)qkv, positions, (const TT*)c, (const TT*)sn, rows, (T*)q_out, (T*)kc, (T*)vc,
-        batch, seq, h, hkv, d, max_batch, max_seq, seq_base, seq_cap, total_rows, head_group, groups);
+  const int64_t work = batch * seq * (h + 2 * hkv) * (d / 2 / VEC);
+  rope_kv_append_kernel<T, TT, VEC><<<(unsigned)((work + threads - 1) / threads), threads, 0, s>>>(
+      (const T*)qkv, positions, (const TT*)c, (const TT*)sn, rows, (T*)q_out, (T*)kc, (T*)vc, batch,
+      seq, h, hkv, d, max_batch, max_seq, seq_base, seq_cap, total_rows);
   return lpc::check_launch("rope_kv_append");
 }
 

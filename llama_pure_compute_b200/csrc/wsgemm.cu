@@ -453,12 +453,14 @@ __device__ __forceinline__ void reduce_slice_any(uint32_t prow, int swz, int c0,
 // No atomics, no global workspace.
 //
 // NORM: the activations are the raw rows x of an RMSNorm whose weight is
-// folded into the packed weights (lpc_pack_weights' k_scale).  While the main
-// loop runs, the epilogue warps read every activation tile the MMA consumes
-// from shared memory and accumulate each token row's sum of squares (the
-// stage is released only after both the MMA and these reads are done); the
-// split ranks add their partial sums through distributed shared memory, and
-// the epilogue multiplies each token's accumulators by rsqrt(sum / K + eps):
+// folded into the packed weights (lpc_pack_weights' k_scale).  The producer
+// warp reads each activation tile once the MMA has consumed it -- right
+// before it refills that stage, and for the last stages after issuing its
+// final copies -- and accumulates each token row's sum of squares (one lane
+// per row, all 8 chunks of it); the sums go to shared memory behind the
+// `stats` barrier.  The split ranks add their partial sums through
+// distributed shared memory, and the epilogue multiplies each token's
+// accumulators by rsqrt(sum / K + eps):
 // norm(x) W^T = rsqrt(mean(x^2) + eps) * (x (W diag(w))^T).
 template <typename T, int EPI, bool NORM>
 __global__ void __launch_bounds__(THREADS, 2)
@@ -474,13 +476,14 @@ __global__ void __launch_bounds__(THREADS, 2)
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (stages + s); };
   const uint32_t accum = bars + 8u * (2 * stages);
-  const uint32_t tmem_slot = accum + 8u;
+  const uint32_t stats_bar = accum + 8u;  // NORM: the producer's row sums are in `ssq`
+  const uint32_t tmem_slot = accum + 16u;
   volatile uint32_t* tmem_slot_ptr =
       reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
   // EPI_QKV token table (TOK_TABLE_BYTES past the barriers), then for NORM
   // the per-token sums of squares and row scales (MAX_TOKENS floats each)
-  TokSlot* tab = reinterpret_cast<TokSlot*>(smem_raw + (tmem_slot + 16u - raw));
-  const uint32_t ssq_addr = tmem_slot + 16u + (EPI == EPI_QKV ? (uint32_t)TOK_TABLE_BYTES : 0u);
+  TokSlot* tab = reinterpret_cast<TokSlot*>(smem_raw + (tmem_slot + 8u - raw));
+  const uint32_t ssq_addr = tmem_slot + 8u + (EPI == EPI_QKV ? (uint32_t)TOK_TABLE_BYTES : 0u);
   float* ssq = reinterpret_cast<float*>(smem_raw + (ssq_addr - raw));
   float* rt = ssq + MAX_TOKENS;
 
@@ -507,11 +510,10 @@ __global__ void __launch_bounds__(THREADS, 2)
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       lpc::mbar_init(full_bar(s), 1);
-      // a stage is free once the MMA has read it, and with NORM once the four
-      // epilogue warps have read its activation rows
-      lpc::mbar_init(empty_bar(s), NORM ? 5 : 1);
+      lpc::mbar_init(empty_bar(s), 1);
     }
     lpc::mbar_init(accum, 1);
+    lpc::mbar_init(stats_bar, 1);
     lpc::fence_mbar_init();
     lpc::tma_prefetch_desc(&tmX);
     // The first round of stages needs no empty-slot wait, and the packed
@@ -534,15 +536,71 @@ __global__ void __launch_bounds__(THREADS, 2)
   const uint32_t tmem = *tmem_slot_ptr;
 
   if (warp == 0) {
-    if (lane == 0) {
-      for (int i = first; i < nkb; ++i) {
-        if (!lpc::mbar_wait(empty_bar(i % stages), ((uint32_t)(i / stages) & 1u) ^ 1u, st)) break;
-        load_w(i);
-        load_x(i);
+    if (!NORM) {
+      if (lane == 0) {
+        for (int i = first; i < nkb; ++i) {
+          if (!lpc::mbar_wait(empty_bar(i % stages), ((uint32_t)(i / stages) & 1u) ^ 1u, st)) break;
+          load_w(i);
+          load_x(i);
+        }
+        // every load of this CTA is issued and its TMEM is allocated: the next
+        // grid may start its prologue
+        lpc::pdl_trigger();
       }
-      // every load of this CTA is issued and its TMEM is allocated: the next
-      // grid may start its prologue
-      lpc::pdl_trigger();
+    } else {
+      // rows lane, lane + 32, ... of every activation tile; lane l starts at
+      // chunk l % 8, so the lanes of a quarter-warp hit all 32 banks
+      float acc[MAX_TOKENS / 32];
+#pragma unroll
+      for (int j = 0; j < MAX_TOKENS / 32; ++j) acc[j] = 0.f;
+      auto row_sums = [&](int i) {  // k-block i, landed in its stage
+        const uint32_t xb = base + (uint32_t)(i % stages) * stage_bytes + CHUNK;
+#pragma unroll
+        for (int j = 0; j < MAX_TOKENS / 32; ++j) {
+          const int row = lane + 32 * j;
+          if (row < NT) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              acc[j] += sumsq8<T>(ld_shared_v4(xb + (uint32_t)(row * 128 + ((c + lane) & 7) * 16)));
+          }
+        }
+      };
+      // k-block j is summed once its tile has landed (full barrier), one
+      // iteration after the refill that follows it was issued, so the reads
+      // stay off the refill's critical path; it is always summed before its
+      // stage is refilled.  Every lane waits: a converged warp sleeps in the
+      // wait, where one polling lane with 31 parked ones keeps issuing.
+      bool ok = true;
+      int next = 0;  // next k-block to sum
+      auto sum_upto = [&](int last) {
+        for (; next <= last && ok; ++next) {
+          ok = __all_sync(0xffffffffu,
+                          lpc::mbar_wait(full_bar(next % stages), (uint32_t)(next / stages) & 1u, st));
+          if (ok) row_sums(next);
+        }
+      };
+      sum_upto(first - stages);
+      for (int i = first; i < nkb && ok; ++i) {
+        ok = __all_sync(0xffffffffu,
+                        lpc::mbar_wait(empty_bar(i % stages), ((uint32_t)(i / stages) & 1u) ^ 1u, st));
+        if (!ok) break;
+        __syncwarp();
+        if (lane == 0) {
+          // this warp's reads of the stage come before the copy that refills it
+          lpc::fence_proxy_async_smem();
+          load_w(i);
+          load_x(i);
+        }
+        __syncwarp();
+        sum_upto(i - stages + 1);
+      }
+      if (lane == 0) lpc::pdl_trigger();
+      sum_upto(nkb - 1);
+#pragma unroll
+      for (int j = 0; j < MAX_TOKENS / 32; ++j)
+        if (lane + 32 * j < NT) ssq[lane + 32 * j] = ok ? acc[j] : 0.f;
+      __syncwarp();
+      if (lane == 0) lpc::mbar_arrive(stats_bar);
     }
   } else if (warp == 2) {
     if (lane == 0) {
@@ -573,46 +631,10 @@ __global__ void __launch_bounds__(THREADS, 2)
     }
     bool stats_ok = true;
     if (NORM) {
-      // thread t reads 16-byte chunk t % 8 of token rows t / 8 + 16 j of
-      // every activation tile (rows are 128 bytes; the swizzle only permutes
-      // chunks within a row, so the row sums are unaffected)
-      const int tid = (int)threadIdx.x - 128;
-      const int pch = tid & 7, r0 = tid >> 3;
-      const int nrow = NT >> 4;
-      float acc[MAX_TOKENS / 16];
-#pragma unroll
-      for (int j = 0; j < MAX_TOKENS / 16; ++j) acc[j] = 0.f;
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % stages;
-        // one lane per warp waits (a warp of pollers would contend with the
-        // producer and the MMA issuer for the barrier); the warp follows it
-        bool got = true;
-        if (lane == 0) got = lpc::mbar_wait(full_bar(s), (uint32_t)(i / stages) & 1u, st);
-        if (!__shfl_sync(0xffffffffu, got, 0)) {
-          stats_ok = false;
-          break;
-        }
-        const uint32_t xb = base + (uint32_t)s * stage_bytes + CHUNK + (uint32_t)(pch * 16 + r0 * 128);
-#pragma unroll
-        for (int j = 0; j < MAX_TOKENS / 16; ++j)
-          if (j < nrow) acc[j] += sumsq8<T>(ld_shared_v4(xb + (uint32_t)(j * 16 * 128)));
-        __syncwarp();
-        if (lane == 0) lpc::mbar_arrive(empty_bar(s));
-      }
-#pragma unroll
-      for (int j = 0; j < MAX_TOKENS / 16; ++j) {
-        acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], 1);
-        acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], 2);
-        acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], 4);
-      }
-      if (pch == 0) {
-#pragma unroll
-        for (int j = 0; j < MAX_TOKENS / 16; ++j)
-          if (j < nrow) ssq[r0 + 16 * j] = acc[j];
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      // the producer's row sums of squares
+      stats_ok = __all_sync(0xffffffffu, lpc::mbar_wait(stats_bar, 0, st));
       if (splits == 1) {
-        for (int t = tid; t < NT; t += 128) rt[t] = rsqrtf(ssq[t] / (float)K + eps);
+        for (int t = (int)threadIdx.x - 128; t < NT; t += 128) rt[t] = rsqrtf(ssq[t] / (float)K + eps);
         asm volatile("bar.sync 1, 128;" ::: "memory");
       }
     }

@@ -10,22 +10,24 @@ checkpoints and call sites carry over.  What runs underneath:
   RoPE + KV append  -> lpc_rope_kv_append (model.py:146-168 fused into one kernel;
                        per-row positions, so batches may be ragged)
                        decode steps of <= FUSED_QKV_MAX_TOKENS tokens (head_dim
-                       128): input norm, projection, RoPE and KV append in one
-                       kernel, lpc_qkv_rope_append, on a packed copy of the
-                       q/k/v weight with the norm weight folded in
+                       128): projection, RoPE and KV append in one kernel,
+                       lpc_qkv_rope_append, on a packed copy of the q/k/v
+                       weight (with ``norm_in_gemm`` the input norm too, its
+                       weight folded into the copy)
   attention         -> decode: lpc_decode_attention over device seq_lens
                        (no per-layer .item() sync, model.py:159-161);
                        prefill / no cache: lpc_flash_attention (tcgen05)
   o_proj + residual -> one addmm (residual added in the GEMM epilogue); decode
                        steps of <= PACKED_RESIDUAL_MAX_TOKENS tokens: lpc_wsgemm
                        (residual epilogue) on a packed copy of o_proj
-  post norm + SwiGLU-> lpc_rmsswiglu_folded_forward (model.py:315-321): the norm
-                       inside the CTA-pair tcgen05 GEMM with the SiLU*up
-                       epilogue, on gate/up with the norm weight folded in (no
-                       torch.cat of weights, no normalised copy in HBM);
-                       decode steps of <= 128 tokens: the norm and SiLU*up in
-                       one lpc_wsgemm on a packed copy of gate/up (norm weight
-                       folded in)
+  post norm + SwiGLU-> lpc_rmsswiglu_forward (model.py:315-321; row norm, then
+                       the tcgen05 GEMM with the SiLU*up epilogue launched
+                       under it, no torch.cat of weights), or with
+                       ``fuse_mlp_norm`` lpc_rmsswiglu_folded_forward (the norm
+                       inside the CTA-pair GEMM on gate/up with the norm weight
+                       folded in); decode steps of <= 128 tokens: row norm +
+                       lpc_wsgemm on a packed copy of gate/up (with
+                       ``norm_in_gemm`` one lpc_wsgemm, norm weight folded)
   down + residual   -> one addmm; decode steps of <= PACKED_RESIDUAL_MAX_TOKENS
                        tokens: lpc_wsgemm (residual epilogue), packed down_proj
   lm_head           -> all positions by default (model.py:475), or only the
@@ -55,10 +57,13 @@ PACKED_SWIGLU_MAX_TOKENS = 128
 # Decode steps with at most this many tokens run the input norm, the q/k/v
 # projection, RoPE and the KV append in one kernel (lpc_qkv_rope_append) on a
 # packed copy of the q/k/v weight, built on first use.
-FUSED_QKV_MAX_TOKENS = 64
+FUSED_QKV_MAX_TOKENS = 32
 # Decode steps with at most this many tokens run o_proj and down_proj with the
-# residual add on packed copies of their weights (lpc_wsgemm).
-PACKED_RESIDUAL_MAX_TOKENS = 32
+# residual add on packed copies of their weights (lpc_wsgemm).  Off by
+# default: faster than cuBLAS in isolation at 32 tokens (13.7 against
+# 14.9 us for o_proj, 22.2 against 25.0 for down_proj) but 2% slower per
+# decode step at 32 sequences (4.60 against 4.52 ms).
+PACKED_RESIDUAL_MAX_TOKENS = 0
 
 __all__ = ["precompute_freqs_cis", "LlamaAttention", "LlamaDecodeLayer", "LlamaModel",
            "LlamaForCausalLM"]
@@ -90,7 +95,8 @@ class _StepContext:
     """Per-forward data shared by all layers (computed once, not per layer)."""
 
     __slots__ = ("positions", "seq_lens", "start_pos", "cos_table", "sin_table", "decode",
-                 "workspace", "packed_max", "fused_qkv_max", "resid_max", "fuse_norm")
+                 "workspace", "packed_max", "fused_qkv_max", "resid_max", "fuse_norm",
+                 "norm_in_gemm")
 
     def __init__(self):
         self.positions = None
@@ -102,7 +108,8 @@ class _StepContext:
         self.packed_max = 0
         self.fused_qkv_max = 0
         self.resid_max = 0
-        self.fuse_norm = True
+        self.fuse_norm = False
+        self.norm_in_gemm = False
         self.workspace = None
 
 
@@ -234,7 +241,7 @@ class LlamaAttention(nn.Module):
 
     def fuses_input_norm(self, x: torch.Tensor, ctx: Optional[_StepContext]) -> bool:
         """Whether this step's input norm runs inside the q/k/v kernel."""
-        return self._fused_qkv(x, ctx)
+        return ctx is not None and ctx.norm_in_gemm and self._fused_qkv(x, ctx)
 
     def project_out(self, attn: torch.Tensor, residual: torch.Tensor,
                     ctx: Optional[_StepContext] = None) -> torch.Tensor:
@@ -268,16 +275,17 @@ class LlamaDecodeLayer(nn.Module):
         self._folded = None
         self._folded_key = None
 
-    def packed_gate_up(self):
-        """gate/up weights in the packed SwiGLU tile layout (lpc_pack_weights)
-        with the post-attention norm weight folded in; built on first use and
-        rebuilt when a weight changes."""
+    def packed_gate_up(self, fold_norm: bool = False):
+        """gate/up weights in the packed SwiGLU tile layout (lpc_pack_weights),
+        with the post-attention norm weight folded in when ``fold_norm``; built
+        on first use and rebuilt when a weight changes."""
         from .packed_linear import PackedWeight
         nw = self.post_attention_layernorm.weight
         ws = (self.gate_proj.weight, self.up_proj.weight, nw)
-        key = tuple(_weight_key(w) for w in ws)
+        key = tuple(_weight_key(w) for w in ws) + (fold_norm,)
         if self._packed_gate_up is None or key != self._packed_key:
-            self._packed_gate_up = PackedWeight(ws[0], ws[1], layout="swiglu", norm_weight=nw)
+            self._packed_gate_up = PackedWeight(ws[0], ws[1], layout="swiglu",
+                                                norm_weight=nw if fold_norm else None)
             self._packed_key = key
         return self._packed_gate_up
 
@@ -312,15 +320,20 @@ class LlamaDecodeLayer(nn.Module):
             self._folded_key = key
         return self._folded
 
-    def _mlp_inter(self, h: torch.Tensor, packed_max: int, fuse_norm: bool = True) -> torch.Tensor:
+    def _mlp_inter(self, h: torch.Tensor, packed_max: int, fuse_norm: bool = False,
+                   norm_in_gemm: bool = False) -> torch.Tensor:
         norm = self.post_attention_layernorm
         tokens = h.numel() // h.shape[-1]
         if tokens <= packed_max and _packable(h, self.gate_proj.weight):
-            # decode-sized: the norm and SiLU*up in one weight-streaming GEMM
-            # on the packed gate/up (norm weight folded in; each token's
-            # rsqrt(mean(h^2) + eps) taken inside the kernel)
+            # decode-sized: the weight-streaming GEMM on the packed gate/up with
+            # the SiLU*up epilogue; the norm either in its own kernel (faster on
+            # B200, see norm_in_gemm) or inside the GEMM on the folded weight
             from .packed_linear import packed_linear
-            return packed_linear(h, self.packed_gate_up(), "swiglu", norm_eps=norm.eps)
+            if norm_in_gemm:
+                return packed_linear(h, self.packed_gate_up(True), "swiglu", norm_eps=norm.eps)
+            from .ops import rmsnorm_forward
+            return packed_linear(rmsnorm_forward(h, norm.weight, norm.eps), self.packed_gate_up(),
+                                 "swiglu")
         if (fuse_norm and _packable(h, self.gate_proj.weight)
                 and self.gate_proj.weight.shape[0] % 16 == 0):
             folded = self.folded_gate_up()
@@ -364,7 +377,8 @@ class LlamaDecodeLayer(nn.Module):
                                   kv_cache=kv_cache, layer_idx=self.layer_idx, mask=mask, ctx=ctx)
         h = self.self_attn.project_out(attn, x, ctx)
         mlp_inter = self._mlp_inter(h, ctx.packed_max if ctx is not None and ctx.decode else 0,
-                                    ctx.fuse_norm if ctx is not None else True)
+                                    ctx.fuse_norm if ctx is not None else False,
+                                    ctx.norm_in_gemm if ctx is not None else False)
         return self._down(mlp_inter, h, ctx)
 
 
@@ -387,10 +401,22 @@ class LlamaModel(nn.Module):
         # decode steps with at most this many tokens run o_proj / down_proj
         # with the residual on packed copies (0 disables them)
         self.packed_residual_max_tokens = PACKED_RESIDUAL_MAX_TOKENS
-        # larger steps run the post-attention norm inside the SwiGLU GEMM on
-        # gate/up weights with the norm weight folded in (a folded copy is made
-        # only when that weight is not all ones); False: separate norm kernel
-        self.fuse_mlp_norm = True
+        # True: steps above packed_swiglu_max_tokens run the post-attention
+        # norm inside the CTA-pair SwiGLU GEMM (lpc_rmsswiglu_folded_forward,
+        # on gate/up with the norm weight folded in; a folded copy is made only
+        # when that weight is not all ones).  False (default): the row-norm
+        # kernel, then the GEMM, launched under it -- measured 1% faster per
+        # decode step at 256 sequences, where the separate norm's early launch
+        # trigger lets the GEMM's weight stream start under it.
+        self.fuse_mlp_norm = False
+        # True: decode-sized steps normalise inside the weight-streaming GEMMs
+        # (q/k/v + RoPE + append, SwiGLU) from the activation tiles, norm
+        # weights folded into the packed copies.  False (default): a row-norm
+        # kernel before each.  Reading the TMA-written activation tiles with
+        # ordinary loads while the copies stream slowed the 32-token SwiGLU
+        # GEMM from 30 to 53-63 us on B200, more than the 5 us the separate
+        # norm costs.
+        self.norm_in_gemm = False
 
     def reset_rope_tables(self) -> None:
         """Recompute cos/sin (e.g. after materialising a meta-device model)."""
@@ -417,6 +443,7 @@ class LlamaModel(nn.Module):
         ctx.fused_qkv_max = self.fused_qkv_max_tokens
         ctx.resid_max = self.packed_residual_max_tokens
         ctx.fuse_norm = self.fuse_mlp_norm
+        ctx.norm_in_gemm = self.norm_in_gemm
         cos = sin = None
         if kv_cache is not None:
             ctx.cos_table, ctx.sin_table = self.cos_cached, self.sin_cached
