@@ -562,33 +562,39 @@ def measure_kernels(dev, only=None):
         if want("swiglu_pair") or want("wsgemm_swiglu"):
             ws = [rn(2 * I, D, std=0.02) for _ in range(6)]
         if want("swiglu_pair"):
-            # SwiGLU of the 7B layer at 256 tokens: the norm inside the
-            # CTA-pair tcgen05 GEMM (norm weight folded into gate/up)
+            # SwiGLU of the 7B layer at 256 tokens: row norm + CTA-pair tcgen05
+            # GEMM launched under it (the decode step's path), and the one-kernel
+            # form with the norm inside (norm weight folded into gate/up)
             M = 256
             x = rn(M, D)
+            empty = torch.empty(0, device=dev, dtype=bf)
+            us = _time_rotating([lambda w=w: ops.rmsswiglu_forward(x, w1, w, empty, 1e-5)
+                                 for w in ws])
+            out.append(_kentry("rmsnorm_vec_kernel + swiglu_pair_kernel", "7B gate/up, 256 tokens",
+                               us, nbytes=2 * I * D * 2 + M * D * 2 + M * I * 2,
+                               flops=2 * M * D * 2 * I, hbm=hbm, tc=tc, timing=steady))
             us = _time_rotating([lambda w=w: ops.rmsswiglu_folded_forward(x, w, None, 1e-5)
                                  for w in ws])
             out.append(_kentry("swiglu_pair_kernel (norm inside)", "7B gate/up, 256 tokens", us,
                                nbytes=2 * I * D * 2 + M * D * 2 + M * I * 2,
                                flops=2 * M * D * 2 * I, hbm=hbm, tc=tc, timing=steady))
         if want("wsgemm_swiglu"):
-            # decode-sized norm + SwiGLU on packed weights (32 tokens)
-            pws = [PackedWeight(w, layout="swiglu", norm_weight=w1) for w in ws]
+            # decode-sized SwiGLU on packed weights (32 tokens, normed input)
+            pws = [PackedWeight(w, layout="swiglu") for w in ws]
             M = 32
             x = rn(M, D)
-            us = _time_rotating([lambda pw=pw: packed_linear(x, pw, "swiglu", norm_eps=1e-5)
-                                 for pw in pws])
-            out.append(_kentry("wsgemm_kernel (norm + SwiGLU epilogue)", "7B gate/up, 32 tokens",
+            us = _time_rotating([lambda pw=pw: packed_linear(x, pw, "swiglu") for pw in pws])
+            out.append(_kentry("wsgemm_kernel (SwiGLU epilogue)", "7B gate/up, 32 tokens",
                                us, nbytes=2 * I * D * 2 + M * D * 2 + M * I * 2, hbm=hbm, tc=tc,
                                timing=steady))
             del pws
         if want("swiglu_pair") or want("wsgemm_swiglu"):
             del ws
         if want("wsgemm_qkv"):
-            # input norm + q/k/v projection + RoPE + KV append (32 tokens)
+            # q/k/v projection + RoPE + KV append (32 tokens, normed input)
             M = 32
             wq = [rn(3 * H * 128, D, std=0.02) for _ in range(6)]
-            pq = [PackedWeight(w, layout="heads", norm_weight=w1) for w in wq]
+            pq = [PackedWeight(w, layout="heads") for w in wq]
             cos, sin = precompute_freqs_cis(128, 1024, device=dev)
             cos, sin = cos.to(bf), sin.to(bf)
             x = rn(M, 1, D)
@@ -596,8 +602,8 @@ def measure_kernels(dev, only=None):
             kc = torch.zeros(M, H, 1024, 128, device=dev, dtype=bf)
             vc = torch.zeros_like(kc)
             us = _time_rotating([lambda pw=pw: ops.qkv_rope_append(x, pw, pos, cos, sin, kc, vc, H,
-                                                                   H, norm_eps=1e-5) for pw in pq])
-            out.append(_kentry("wsgemm_kernel (EPI_QKV: norm + projection + RoPE + KV append)",
+                                                                   H) for pw in pq])
+            out.append(_kentry("wsgemm_kernel (EPI_QKV: projection + RoPE + KV append)",
                                "7B q/k/v, 32 tokens", us,
                                nbytes=3 * H * 128 * D * 2 + M * D * 2 + M * 3 * H * 128 * 2,
                                hbm=hbm, tc=tc, timing=steady))
