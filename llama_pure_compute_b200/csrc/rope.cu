@@ -13,6 +13,8 @@
 //
 // Each thread owns VEC consecutive rotation pairs of one (token, head): it
 // loads the VEC lower-half and VEC upper-half elements as 16-byte vectors.
+#include <algorithm>
+
 #include "lpc_common.cuh"
 
 LPC_DECLARE_STATUS(g_rope_status)
@@ -151,27 +153,44 @@ __global__ void __launch_bounds__(256) rope_kernel(T* q, T* k, const TT* __restr
 
 // Fused prologue: qkv [B, S, (H + 2Hkv) * D] -> q_out [B, H, S, D] (rotated),
 // key_cache[b, h, pos] (rotated), value_cache[b, h, pos] (copied).
-template <typename T, typename TT, int VEC>
-__global__ void __launch_bounds__(256) rope_kv_append_kernel(
+//
+// A CTA handles one token (blockIdx.x) and K * hpb of its heads (blockIdx.y
+// picks which).  An item is VEC rotation pairs (chunk c) of one head: two
+// 16-byte loads, at d and d + D/2.  The block has chunks * hpb threads;
+// thread t owns chunk t % chunks of heads t / chunks + k * hpb (k < K), chunk
+// fastest, so a warp reads contiguous qkv bytes and writes whole 128-byte
+// lines of q / cache rows.  The thread issues its K item loads first, then
+// reads the token's position and its chunk's four cos/sin vectors once for
+// all K items: no per-item index division, no shared memory, no barrier.
+constexpr int RA_THREADS = 256;  // block size at most (chunks * hpb)
+
+template <typename T, typename TT, int VEC, int K>
+__global__ void __launch_bounds__(RA_THREADS, 3) rope_kv_append_kernel(
     const T* __restrict__ qkv, const int64_t* __restrict__ positions, const TT* __restrict__ cosb,
     const TT* __restrict__ sinb, int64_t table_rows, T* __restrict__ q_out,
-    T* __restrict__ kcache, T* __restrict__ vcache, int64_t batch, int64_t seq, int num_heads,
-    int num_kv_heads, int head_dim, int64_t max_batch, int64_t max_seq_len,
+    T* __restrict__ kcache, T* __restrict__ vcache, int64_t seq, int num_heads, int num_kv_heads,
+    int head_dim, int chunks, int hpb, int64_t max_batch, int64_t max_seq_len,
     const int64_t* __restrict__ seq_base, const int32_t* __restrict__ seq_cap, int64_t total_rows) {
   const int half = head_dim >> 1;
-  const int chunks = half / VEC;
   const int heads_all = num_heads + 2 * num_kv_heads;
-  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t work = batch * seq * heads_all * chunks;
-  if (gid >= work) return;
-  const int c = (int)(gid % chunks);
-  const int64_t th = gid / chunks;
-  const int hh = (int)(th % heads_all);
-  const int64_t tok = th / heads_all;  // b * seq + s
-  const int64_t b = tok / seq;
-  const int64_t s = tok - b * seq;
+  const int64_t tok = blockIdx.x;  // b * seq + s
+  const int c = (int)threadIdx.x % chunks;
+  const int hh0 = (int)threadIdx.x / chunks + (int)blockIdx.y * K * hpb;
+  const int d = c * VEC;
+  const T* src = qkv + tok * (int64_t)heads_all * head_dim + d;
+  uint4 x0[K], x1[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int hh = hh0 + k * hpb;
+    if (hh < heads_all) {
+      const T* p = src + (int64_t)hh * head_dim;
+      x0[k] = __ldg(reinterpret_cast<const uint4*>(p));
+      x1[k] = __ldg(reinterpret_cast<const uint4*>(p + half));
+    }
+  }
   const int64_t pos = __ldg(positions + tok);
   if (pos < 0) return;
+  const int64_t b = tok / seq;
   // cache row of (b, kv head 0, pos) and the distance between kv heads:
   //   dense  [max_batch, Hkv, max_seq_len, D]: (b * Hkv) * max_seq_len + pos, max_seq_len
   //   ragged [Hkv, total_rows, D] (seq_base != nullptr): seq_base[b] + pos, total_rows
@@ -189,40 +208,47 @@ __global__ void __launch_bounds__(256) rope_kv_append_kernel(
     head_rows = total_rows;
   }
   if (!ok || pos >= table_rows) {
-    atomicOr(&g_rope_status, LPC_DEV_ERR_BOUNDS);
+    if (threadIdx.x == 0) atomicOr(&g_rope_status, LPC_DEV_ERR_BOUNDS);
     return;
   }
-  const int d = c * VEC;
-  const T* src = qkv + tok * (int64_t)heads_all * head_dim + (int64_t)hh * head_dim;
-  float x0[VEC], x1[VEC];
-  load_f<T, VEC>(src + d, x0);
-  load_f<T, VEC>(src + d + half, x1);
-
-  if (hh >= num_heads + num_kv_heads) {  // V: plain copy into the cache
-    const int h = hh - num_heads - num_kv_heads;
-    T* dst = vcache + (row + h * head_rows) * (int64_t)head_dim;
-    store_f<T, VEC>(dst + d, x0);
-    store_f<T, VEC>(dst + d + half, x1);
-    return;
-  }
+  const int rot_heads = num_heads + num_kv_heads;  // q and k heads come before v
   float c0[VEC], s0[VEC], c1[VEC], s1[VEC];
-  const TT* cr = cosb + pos * (int64_t)head_dim;
-  const TT* sr = sinb + pos * (int64_t)head_dim;
-  load_f<TT, VEC>(cr + d, c0);
-  load_f<TT, VEC>(sr + d, s0);
-  load_f<TT, VEC>(cr + d + half, c1);
-  load_f<TT, VEC>(sr + d + half, s1);
-  float o0[VEC], o1[VEC];
-  rotate<VEC>(x0, x1, c0, s0, c1, s1, o0, o1);
-  T* dst;
-  if (hh < num_heads) {
-    dst = q_out + ((b * num_heads + hh) * seq + s) * (int64_t)head_dim;
-  } else {
-    const int h = hh - num_heads;
-    dst = kcache + (row + h * head_rows) * (int64_t)head_dim;
+  if (hh0 < rot_heads) {  // the thread's first head is its lowest
+    const TT* cr = cosb + pos * (int64_t)head_dim;
+    const TT* sr = sinb + pos * (int64_t)head_dim;
+    load_f<TT, VEC>(cr + d, c0);
+    load_f<TT, VEC>(sr + d, s0);
+    load_f<TT, VEC>(cr + d + half, c1);
+    load_f<TT, VEC>(sr + d + half, s1);
   }
-  store_f<T, VEC>(dst + d, o0);
-  store_f<T, VEC>(dst + d + half, o1);
+  const int64_t q_row = (b * num_heads) * seq + (tok - b * seq);  // q_out row of (b, head 0, s)
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int hh = hh0 + k * hpb;
+    if (hh >= heads_all) continue;
+    if (hh >= rot_heads) {  // V: plain copy into the cache
+      T* dst = vcache + (row + (int64_t)(hh - rot_heads) * head_rows) * head_dim;
+      reinterpret_cast<uint4*>(dst + d)[0] = x0[k];
+      reinterpret_cast<uint4*>(dst + d + half)[0] = x1[k];
+      continue;
+    }
+    float a0[VEC], a1[VEC];
+    {
+      const T* e0 = reinterpret_cast<const T*>(&x0[k]);
+      const T* e1 = reinterpret_cast<const T*>(&x1[k]);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        a0[i] = Num<T>::to_f(e0[i]);
+        a1[i] = Num<T>::to_f(e1[i]);
+      }
+    }
+    float o0[VEC], o1[VEC];
+    rotate<VEC>(a0, a1, c0, s0, c1, s1, o0, o1);
+    T* dst = hh < num_heads ? q_out + (q_row + (int64_t)hh * seq) * head_dim
+                            : kcache + (row + (int64_t)(hh - num_heads) * head_rows) * head_dim;
+    store_f<T, VEC>(dst + d, o0);
+    store_f<T, VEC>(dst + d + half, o1);
+  }
 }
 
 template <typename T, typename TT>
@@ -259,17 +285,49 @@ int launch_rope_t(int table_dtype, void* q, void* k, const void* c, const void* 
   return LPC_ERR_UNSUPPORTED;
 }
 
+template <typename T, typename TT, int K>
+void launch_fused_k(dim3 grid, int threads, const void* qkv, const int64_t* positions,
+                    const void* c, const void* sn, int64_t rows, void* q_out, void* kc, void* vc,
+                    int64_t seq, int h, int hkv, int d, int chunks, int hpb, int64_t max_batch,
+                    int64_t max_seq, const int64_t* seq_base, const int32_t* seq_cap,
+                    int64_t total_rows, cudaStream_t s) {
+  constexpr int VEC = 16 / (int)sizeof(T);
+  rope_kv_append_kernel<T, TT, VEC, K><<<grid, threads, 0, s>>>(
+      (const T*)qkv, positions, (const TT*)c, (const TT*)sn, rows, (T*)q_out, (T*)kc, (T*)vc, seq,
+      h, hkv, d, chunks, hpb, max_batch, max_seq, seq_base, seq_cap, total_rows);
+}
+
 template <typename T, typename TT>
 int launch_fused(const void* qkv, const int64_t* positions, const void* c, const void* sn,
                  int64_t rows, void* q_out, void* kc, void* vc, int64_t batch, int64_t seq, int h,
                  int hkv, int d, int64_t max_batch, int64_t max_seq, const int64_t* seq_base,
                  const int32_t* seq_cap, int64_t total_rows, cudaStream_t s) {
   constexpr int VEC = 16 / (int)sizeof(T);
-  const int threads = 256;
-  const int64_t work = batch * seq * (h + 2 * hkv) * (d / 2 / VEC);
-  rope_kv_append_kernel<T, TT, VEC><<<(unsigned)((work + threads - 1) / threads), threads, 0, s>>>(
-      (const T*)qkv, positions, (const TT*)c, (const TT*)sn, rows, (T*)q_out, (T*)kc, (T*)vc, batch,
-      seq, h, hkv, d, max_batch, max_seq, seq_base, seq_cap, total_rows);
+  const int64_t tokens = batch * seq;
+  if (tokens == 0) return LPC_OK;
+  const int chunks = d / 2 / VEC;
+  const int heads_all = h + 2 * hkv;
+  if (chunks > RA_THREADS || tokens > 0x7fffffffLL) {
+    lpc::set_error("rope_kv_append: unsupported shape (tokens=%lld dim=%d)", (long long)tokens, d);
+    return LPC_ERR_UNSUPPORTED;
+  }
+  const int hpb = RA_THREADS / chunks;  // heads per k step
+  const int steps = (heads_all + hpb - 1) / hpb;
+  const int K = steps < 4 ? steps : 4;
+  const dim3 grid((unsigned)tokens, (unsigned)((heads_all + K * hpb - 1) / (K * hpb)));
+  const int threads = chunks * hpb;
+#define LPC_RA(KK)                                                                                 \
+  launch_fused_k<T, TT, KK>(grid, threads, qkv, positions, c, sn, rows, q_out, kc, vc, seq, h, hkv, \
+                            d, chunks, hpb, max_batch, max_seq, seq_base, seq_cap, total_rows, s)
+  if (K == 1)
+    LPC_RA(1);
+  else if (K == 2)
+    LPC_RA(2);
+  else if (K == 3)
+    LPC_RA(3);
+  else
+    LPC_RA(4);
+#undef LPC_RA
   return lpc::check_launch("rope_kv_append");
 }
 

@@ -86,6 +86,28 @@ def test_kv_append_random_slots(dtype, head_dim):
     assert np.array_equal(vd.cpu().view(it).numpy(), vn)
 
 
+@pytest.mark.parametrize("T,H,D,dtype", [(2000, 8, 128, torch.bfloat16), (10, 128, 128, torch.bfloat16),
+                                         (700, 4, 128, torch.float32), (3000, 1, 64, torch.float16)])
+def test_kv_append_token_runs(T, H, D, dtype):
+    """Token counts and head counts that give runs of several tokens per CTA
+    (a few heads), and runs longer than one batch of loads (128 heads)."""
+    g = torch.Generator().manual_seed(T + H)
+    Bmax, S = 8, (T + 7) // 8 + 3
+    slots = torch.randperm(Bmax * S, generator=g)[:T].to(torch.int64)
+    slots[::11] = -1
+    k = torch.randn(T, H, D, generator=g).to(dtype)
+    v = torch.randn(T, H, D, generator=g).to(dtype)
+    kc = torch.randn(Bmax, H, S, D, generator=g).to(dtype)
+    vc = torch.randn(Bmax, H, S, D, generator=g).to(dtype)
+    kd, vd = kc.to(DEV), vc.to(DEV)
+    ops.update_kv_cache(k.to(DEV), v.to(DEV), kd, vd, slots.to(DEV))
+    it = torch.int32 if dtype == torch.float32 else torch.int16
+    kn, vn = kc.view(it).numpy().copy(), vc.view(it).numpy().copy()
+    kv_append_ref(k.view(it).numpy(), v.view(it).numpy(), kn, vn, slots.numpy())
+    assert np.array_equal(kd.cpu().view(it).numpy(), kn)
+    assert np.array_equal(vd.cpu().view(it).numpy(), vn)
+
+
 def test_kv_append_default_slots_and_empty():
     k = torch.randn(3, 2, 128, device=DEV, dtype=torch.bfloat16)
     kc = torch.zeros(2, 2, 4, 128, device=DEV, dtype=torch.bfloat16)
@@ -154,14 +176,15 @@ def test_rope_position_out_of_table_is_flagged():
     assert _lib.device_status() & 0x2
 
 
-@pytest.mark.parametrize("B,S,H,Hkv", [(3, 5, 4, 2), (64, 1, 32, 32), (2, 17, 8, 8)])
+@pytest.mark.parametrize("B,S,H,Hkv", [(3, 5, 4, 2), (64, 1, 32, 32), (2, 17, 8, 8), (4, 300, 4, 2),
+                                       (2, 3, 128, 8), (1, 700, 32, 8)])
 def test_rope_kv_append_bit_exact(B, S, H, Hkv):
     g = torch.Generator().manual_seed(7)
-    D, Smax = 128, 40
+    D, Smax = 128, S + 35
     qkv = torch.randn(B, S, (H + 2 * Hkv) * D, generator=g).to(torch.bfloat16)
     start = torch.randint(0, Smax - S, (B, 1), generator=g)
     pos = start + torch.arange(S).unsqueeze(0)
-    cos, sin = rope_tables(D, 64, 10000.0)
+    cos, sin = rope_tables(D, Smax + 24, 10000.0)
     cos, sin = cos.to(torch.bfloat16), sin.to(torch.bfloat16)
     kc = torch.randn(B, Hkv, Smax, D, generator=g).to(torch.bfloat16)
     vc = torch.randn(B, Hkv, Smax, D, generator=g).to(torch.bfloat16)
@@ -183,6 +206,23 @@ def test_rmsnorm(dtype, tol, rows, dim):
     x = (torch.randn(rows, dim, generator=g) * 2).to(dtype)
     w = (1 + 0.02 * torch.randn(dim, generator=g)).to(dtype)
     y = ops.rmsnorm_forward(x.to(DEV), w.to(DEV), 1e-5).cpu()
+    torch.testing.assert_close(y.float(), rmsnorm_ref(x, w, 1e-5).float(), rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("rows", [1, 150, 600, 1200, 2400, 5000])
+@pytest.mark.parametrize("dim,xd,wd", [(4096, torch.bfloat16, torch.bfloat16),
+                                       (4096, torch.bfloat16, torch.float32),
+                                       (2048, torch.float32, torch.bfloat16),
+                                       (1024, torch.float16, torch.float16),
+                                       (8192, torch.bfloat16, torch.bfloat16)])
+def test_rmsnorm_row_layouts(rows, dim, xd, wd):
+    """Every rows-per-CTA choice (1-8 rows of one, two or four warps) and
+    weight dtypes other than x's, against the oracle at the dtype's bar."""
+    g = torch.Generator().manual_seed(rows * 7 + dim)
+    x = (torch.randn(rows, dim, generator=g) * 2).to(xd)
+    w = (1 + 0.02 * torch.randn(dim, generator=g)).to(wd)
+    y = ops.rmsnorm_forward(x.to(DEV), w.to(DEV), 1e-5).cpu()
+    tol = {torch.float32: 2e-6, torch.bfloat16: 8e-3, torch.float16: 1e-3}[xd]
     torch.testing.assert_close(y.float(), rmsnorm_ref(x, w, 1e-5).float(), rtol=tol, atol=tol)
 
 
