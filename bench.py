@@ -649,7 +649,7 @@ def measure_kernels(dev, only=None):
             # KV append alone (update_kv_cache) at the same size
             us = _time_rotating([lambda t=t: ops.update_kv_cache(t[4], t[5], t[1], t[2])
                                  for t in sets])
-            out.append(_kentry("kv_append_kernel", "8192 tokens x 32 heads x 128 (K and V)", us,
+            out.append(_kentry("kv_append_rows_kernel", "8192 tokens x 32 heads x 128 (K and V)", us,
                                nbytes=2 * 2 * B * S * H * 128 * 2, hbm=hbm, tc=tc, timing=rot))
         if want("rope_kv_append") or want("kv_append"):
             del sets
@@ -657,7 +657,7 @@ def measure_kernels(dev, only=None):
             # row RMSNorm at 8192 x 4096
             xs = [rn(B * S, D) for _ in range(4)]
             us = _time_rotating([lambda t=t: ops.rmsnorm_forward(t, w1, 1e-5) for t in xs])
-            out.append(_kentry("rmsnorm_vec_kernel", "8192 x 4096", us,
+            out.append(_kentry("rmsnorm_warp_kernel", "8192 x 4096", us,
                                nbytes=2 * B * S * D * 2 + D * 2, hbm=hbm, tc=tc, timing=rot))
             del xs
     if want("decode"):
