@@ -115,15 +115,6 @@ __device__ __forceinline__ float sumsq8<__half>(const uint4& u) {
   return s;
 }
 
-__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
-  uint4 r;
-  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "r"(addr)
-               : "memory");
-  return r;
-}
-
 __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
   float r;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(r) : "r"(addr) : "memory");
@@ -453,18 +444,18 @@ __device__ __forceinline__ void reduce_slice_any(uint32_t prow, int swz, int c0,
 // No atomics, no global workspace.
 //
 // NORM: the activations are the raw rows x of an RMSNorm whose weight is
-// folded into the packed weights (lpc_pack_weights' k_scale).  The producer
-// warp reads each activation tile once the MMA has consumed it -- right
-// before it refills that stage, and for the last stages after issuing its
-// final copies -- and accumulates each token row's sum of squares (one lane
-// per row, all 8 chunks of it); the sums go to shared memory behind the
-// `stats` barrier.  The split ranks add their partial sums through
-// distributed shared memory, and the epilogue multiplies each token's
-// accumulators by rsqrt(sum / K + eps):
+// folded into the packed weights (lpc_pack_weights' k_scale).  The epilogue
+// warps, idle during the main loop, read this rank's k-range of every token
+// row from global memory (L2) and sum its squares; the split ranks add their
+// partial sums through distributed shared memory, and the epilogue multiplies
+// each token's accumulators by rsqrt(sum / K + eps):
 // norm(x) W^T = rsqrt(mean(x^2) + eps) * (x (W diag(w))^T).
+// (Summing the shared-memory activation tiles instead, which the tensor core
+// reads through the async proxy, slowed the main loop by half.)
 template <typename T, int EPI, bool NORM>
 __global__ void __launch_bounds__(THREADS, 2)
-    wsgemm_kernel(const __grid_constant__ lpc::TmaDesc tmX, const uint8_t* __restrict__ packed,
+    wsgemm_kernel(const __grid_constant__ lpc::TmaDesc tmX, const T* __restrict__ xg,
+                  const uint8_t* __restrict__ packed,
                   T* out, const T* resid, int M, int K, int n_out, int NT, int stages,
                   uint32_t tmem_cols, uint32_t idesc, int splits, const QkvArgs qa, float eps) {
   extern __shared__ uint8_t smem_raw[];
@@ -476,7 +467,6 @@ __global__ void __launch_bounds__(THREADS, 2)
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (stages + s); };
   const uint32_t accum = bars + 8u * (2 * stages);
-  const uint32_t stats_bar = accum + 8u;  // NORM: the producer's row sums are in `ssq`
   const uint32_t tmem_slot = accum + 16u;
   volatile uint32_t* tmem_slot_ptr =
       reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
@@ -513,7 +503,6 @@ __global__ void __launch_bounds__(THREADS, 2)
       lpc::mbar_init(empty_bar(s), 1);
     }
     lpc::mbar_init(accum, 1);
-    lpc::mbar_init(stats_bar, 1);
     lpc::fence_mbar_init();
     lpc::tma_prefetch_desc(&tmX);
     // The first round of stages needs no empty-slot wait, and the packed
@@ -536,71 +525,15 @@ __global__ void __launch_bounds__(THREADS, 2)
   const uint32_t tmem = *tmem_slot_ptr;
 
   if (warp == 0) {
-    if (!NORM) {
-      if (lane == 0) {
-        for (int i = first; i < nkb; ++i) {
-          if (!lpc::mbar_wait(empty_bar(i % stages), ((uint32_t)(i / stages) & 1u) ^ 1u, st)) break;
-          load_w(i);
-          load_x(i);
-        }
-        // every load of this CTA is issued and its TMEM is allocated: the next
-        // grid may start its prologue
-        lpc::pdl_trigger();
+    if (lane == 0) {
+      for (int i = first; i < nkb; ++i) {
+        if (!lpc::mbar_wait(empty_bar(i % stages), ((uint32_t)(i / stages) & 1u) ^ 1u, st)) break;
+        load_w(i);
+        load_x(i);
       }
-    } else {
-      // rows lane, lane + 32, ... of every activation tile; lane l starts at
-      // chunk l % 8, so the lanes of a quarter-warp hit all 32 banks
-      float acc[MAX_TOKENS / 32];
-#pragma unroll
-      for (int j = 0; j < MAX_TOKENS / 32; ++j) acc[j] = 0.f;
-      auto row_sums = [&](int i) {  // k-block i, landed in its stage
-        const uint32_t xb = base + (uint32_t)(i % stages) * stage_bytes + CHUNK;
-#pragma unroll
-        for (int j = 0; j < MAX_TOKENS / 32; ++j) {
-          const int row = lane + 32 * j;
-          if (row < NT) {
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-              acc[j] += sumsq8<T>(ld_shared_v4(xb + (uint32_t)(row * 128 + ((c + lane) & 7) * 16)));
-          }
-        }
-      };
-      // k-block j is summed once its tile has landed (full barrier), one
-      // iteration after the refill that follows it was issued, so the reads
-      // stay off the refill's critical path; it is always summed before its
-      // stage is refilled.  Every lane waits: a converged warp sleeps in the
-      // wait, where one polling lane with 31 parked ones keeps issuing.
-      bool ok = true;
-      int next = 0;  // next k-block to sum
-      auto sum_upto = [&](int last) {
-        for (; next <= last && ok; ++next) {
-          ok = __all_sync(0xffffffffu,
-                          lpc::mbar_wait(full_bar(next % stages), (uint32_t)(next / stages) & 1u, st));
-          if (ok) row_sums(next);
-        }
-      };
-      sum_upto(first - stages);
-      for (int i = first; i < nkb && ok; ++i) {
-        ok = __all_sync(0xffffffffu,
-                        lpc::mbar_wait(empty_bar(i % stages), ((uint32_t)(i / stages) & 1u) ^ 1u, st));
-        if (!ok) break;
-        __syncwarp();
-        if (lane == 0) {
-          // this warp's reads of the stage come before the copy that refills it
-          lpc::fence_proxy_async_smem();
-          load_w(i);
-          load_x(i);
-        }
-        __syncwarp();
-        sum_upto(i - stages + 1);
-      }
-      if (lane == 0) lpc::pdl_trigger();
-      sum_upto(nkb - 1);
-#pragma unroll
-      for (int j = 0; j < MAX_TOKENS / 32; ++j)
-        if (lane + 32 * j < NT) ssq[lane + 32 * j] = ok ? acc[j] : 0.f;
-      __syncwarp();
-      if (lane == 0) lpc::mbar_arrive(stats_bar);
+      // every load of this CTA is issued and its TMEM is allocated: the next
+      // grid may start its prologue
+      lpc::pdl_trigger();
     }
   } else if (warp == 2) {
     if (lane == 0) {
@@ -629,16 +562,31 @@ __global__ void __launch_bounds__(THREADS, 2)
       build_token_table(tab, qa, M, (int)threadIdx.x - 128);
       asm volatile("bar.sync 1, 128;" ::: "memory");
     }
-    bool stats_ok = true;
     if (NORM) {
-      // the producer's row sums of squares
-      stats_ok = __all_sync(0xffffffffu, lpc::mbar_wait(stats_bar, 0, st));
+      // each token row's sum of squares over this rank's k-range, read from
+      // global memory (L2) while the main loop runs: warp w takes rows w,
+      // w + 4, ..., its lanes stride the row's 16-byte vectors
+      const int ew = warp - 4;
+      const int64_t k_lo = (int64_t)kb0 * KB;
+      const int nv = nkb * KB / 8;
+      for (int row = ew; row < NT; row += 4) {
+        float a = 0.f;
+        if (row < M) {
+          const uint4* src = reinterpret_cast<const uint4*>(xg + (int64_t)row * K + k_lo);
+#pragma unroll 8
+          for (int v = lane; v < nv; v += 32) a += sumsq8<T>(__ldg(src + v));
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        }
+        if (lane == 0) ssq[row] = a;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
       if (splits == 1) {
         for (int t = (int)threadIdx.x - 128; t < NT; t += 128) rt[t] = rsqrtf(ssq[t] / (float)K + eps);
         asm volatile("bar.sync 1, 128;" ::: "memory");
       }
     }
-    const bool ok = lpc::mbar_wait(accum, 0, st) && stats_ok;
+    const bool ok = lpc::mbar_wait(accum, 0, st);
     lpc::tc_fence_after();
     const float* rtp = NORM ? rt : nullptr;
     if (splits == 1) {
@@ -808,7 +756,8 @@ int launch(const void* x, const void* packed, void* out, const void* resid, int6
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = p.splits > 1 ? 2 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, wsgemm_kernel<T, EPI, NORM>, tx, (const uint8_t*)packed,
+  cudaError_t e = cudaLaunchKernelEx(&cfg, wsgemm_kernel<T, EPI, NORM>, tx, (const T*)x,
+                                     (const uint8_t*)packed,
                                      (T*)out, (const T*)resid, (int)M, K, (int)n_out, p.NT,
                                      p.stages, p.tmem_cols, idesc, p.splits, qa, eps);
   if (e != cudaSuccess) {

@@ -12,8 +12,8 @@ checkpoints and call sites carry over.  What runs underneath:
                        decode steps of <= FUSED_QKV_MAX_TOKENS tokens (head_dim
                        128): projection, RoPE and KV append in one kernel,
                        lpc_qkv_rope_append, on a packed copy of the q/k/v
-                       weight (with ``norm_in_gemm`` the input norm too, its
-                       weight folded into the copy)
+                       weight; with ``norm_in_gemm`` (default) the input norm
+                       too, its weight folded into the copy
   attention         -> decode: lpc_decode_attention over device seq_lens
                        (no per-layer .item() sync, model.py:159-161);
                        prefill / no cache: lpc_flash_attention (tcgen05)
@@ -26,8 +26,9 @@ checkpoints and call sites carry over.  What runs underneath:
                        ``fuse_mlp_norm`` lpc_rmsswiglu_folded_forward (the norm
                        inside the CTA-pair GEMM on gate/up with the norm weight
                        folded in); decode steps of <= 128 tokens: row norm +
-                       lpc_wsgemm on a packed copy of gate/up (with
-                       ``norm_in_gemm`` one lpc_wsgemm, norm weight folded)
+                       lpc_wsgemm on a packed copy of gate/up; up to
+                       NORM_IN_GEMM_MAX_TOKENS tokens with ``norm_in_gemm``
+                       (default) one lpc_wsgemm, norm weight folded
   down + residual   -> one addmm; decode steps of <= PACKED_RESIDUAL_MAX_TOKENS
                        tokens: lpc_wsgemm (residual epilogue), packed down_proj
   lm_head           -> all positions by default (model.py:475), or only the
@@ -58,6 +59,13 @@ PACKED_SWIGLU_MAX_TOKENS = 128
 # projection, RoPE and the KV append in one kernel (lpc_qkv_rope_append) on a
 # packed copy of the q/k/v weight, built on first use.
 FUSED_QKV_MAX_TOKENS = 32
+# Decode steps with at most this many tokens (and LlamaModel.norm_in_gemm)
+# normalise inside those packed GEMMs: the epilogue warps sum each token row's
+# squares from global memory while the weights stream, and the norm weight is
+# folded into the packed copy.  32-token SwiGLU 30.0 us against 35.3 for the
+# norm kernel + GEMM, q/k/v 23.0 against 22.5 + the norm; at 128 tokens the
+# rows' re-reads cost more than the norm kernel (49.8 against 43.5 us).
+NORM_IN_GEMM_MAX_TOKENS = 64
 # Decode steps with at most this many tokens run o_proj and down_proj with the
 # residual add on packed copies of their weights (lpc_wsgemm).  Off by
 # default: faster than cuBLAS in isolation at 32 tokens (13.7 against
@@ -241,7 +249,8 @@ class LlamaAttention(nn.Module):
 
     def fuses_input_norm(self, x: torch.Tensor, ctx: Optional[_StepContext]) -> bool:
         """Whether this step's input norm runs inside the q/k/v kernel."""
-        return ctx is not None and ctx.norm_in_gemm and self._fused_qkv(x, ctx)
+        return (ctx is not None and ctx.norm_in_gemm and self._fused_qkv(x, ctx)
+                and x.numel() // x.shape[-1] <= NORM_IN_GEMM_MAX_TOKENS)
 
     def project_out(self, attn: torch.Tensor, residual: torch.Tensor,
                     ctx: Optional[_StepContext] = None) -> torch.Tensor:
@@ -329,7 +338,7 @@ class LlamaDecodeLayer(nn.Module):
             # the SiLU*up epilogue; the norm either in its own kernel (faster on
             # B200, see norm_in_gemm) or inside the GEMM on the folded weight
             from .packed_linear import packed_linear
-            if norm_in_gemm:
+            if norm_in_gemm and tokens <= NORM_IN_GEMM_MAX_TOKENS:
                 return packed_linear(h, self.packed_gate_up(True), "swiglu", norm_eps=norm.eps)
             from .ops import rmsnorm_forward
             return packed_linear(rmsnorm_forward(h, norm.weight, norm.eps), self.packed_gate_up(),
@@ -409,14 +418,12 @@ class LlamaModel(nn.Module):
         # decode step at 256 sequences, where the separate norm's early launch
         # trigger lets the GEMM's weight stream start under it.
         self.fuse_mlp_norm = False
-        # True: decode-sized steps normalise inside the weight-streaming GEMMs
-        # (q/k/v + RoPE + append, SwiGLU) from the activation tiles, norm
-        # weights folded into the packed copies.  False (default): a row-norm
-        # kernel before each.  Reading the TMA-written activation tiles with
-        # ordinary loads while the copies stream slowed the 32-token SwiGLU
-        # GEMM from 30 to 53-63 us on B200, more than the 5 us the separate
-        # norm costs.
-        self.norm_in_gemm = False
+        # True (default): decode steps of at most NORM_IN_GEMM_MAX_TOKENS
+        # tokens normalise inside the weight-streaming GEMMs (q/k/v + RoPE +
+        # append, SwiGLU), norm weights folded into the packed copies: 4.47
+        # against 4.52 ms per decode step at 32 sequences.  False: a row-norm
+        # kernel before each GEMM.
+        self.norm_in_gemm = True
 
     def reset_rope_tables(self) -> None:
         """Recompute cos/sin (e.g. after materialising a meta-device model)."""

@@ -195,6 +195,27 @@ def test_rope_kv_append_bit_exact(B, S, H, Hkv):
     assert torch.equal(kd.cpu(), kc) and torch.equal(vd.cpu(), vc)
 
 
+@pytest.mark.parametrize("D,H,Hkv", [(64, 8, 2), (32, 16, 4), (96, 12, 4)])
+def test_rope_kv_append_head_dims(D, H, Hkv):
+    """Other head dims: 4, 2 and 6 chunks of 8 rotation pairs per head, so
+    64, 128 and 42 heads per block step (a 252-thread block for 96)."""
+    g = torch.Generator().manual_seed(D)
+    B, S, Smax = 3, 37, 64
+    qkv = torch.randn(B, S, (H + 2 * Hkv) * D, generator=g).to(torch.bfloat16)
+    pos = torch.randint(0, Smax - S, (B, 1), generator=g) + torch.arange(S).unsqueeze(0)
+    pos[1, 5] = -1  # skipped token
+    cos, sin = rope_tables(D, Smax, 10000.0)
+    cos, sin = cos.to(torch.bfloat16), sin.to(torch.bfloat16)
+    kc = torch.randn(B, Hkv, Smax, D, generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, Hkv, Smax, D, generator=g).to(torch.bfloat16)
+    kd, vd = kc.to(DEV), vc.to(DEV)
+    q = ops.rope_kv_append(qkv.to(DEV), pos.to(DEV), cos.to(DEV), sin.to(DEV), kd, vd, H, Hkv)
+    qr = rope_kv_append_ref(qkv, pos, cos, sin, kc, vc, H, Hkv)
+    valid = (pos >= 0).view(B, 1, S, 1).expand_as(qr)
+    assert torch.equal(q.cpu()[valid], qr[valid])
+    assert torch.equal(kd.cpu(), kc) and torch.equal(vd.cpu(), vc)
+
+
 # ---------------------------------------------------------------------------
 # RMSNorm
 # ---------------------------------------------------------------------------
