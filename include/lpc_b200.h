@@ -298,9 +298,11 @@ LPC_API int lpc_pack_weights(const void* w0, const void* w1, const float* k_scal
  * norm_eps > 0 fuses the RMSNorm that feeds the projection (triton_kernels/
  * rmsnorm.py:58-96): x are the raw rows, the norm weight is folded into the
  * packed weight (lpc_pack_weights' k_scale), and every token's accumulators
- * are scaled by rsqrt(mean(x^2) + norm_eps) -- the sums of squares are taken
- * from the activation tiles the MMA reads, so no normalised copy of x is
- * written.  norm_eps = 0: x is used as given.
+ * are scaled by rsqrt(mean(x^2) + norm_eps) -- the sums of squares are read
+ * by the kernel's epilogue warps from x in global memory while the weights
+ * stream, so no normalised copy of x is written.  Fastest up to about 64
+ * tokens (each CTA re-reads its k-range of every row).  norm_eps = 0: x is
+ * used as given.
  * Split k: when there are few weight tiles the launch runs clusters of up to
  * 8 CTAs per tile, each on a share of k, reduce-scattered through
  * distributed shared memory (deterministic: fixed rank order).  Launched with
