@@ -27,6 +27,8 @@
 //              kernel merges the splits.
 #include <atomic>
 
+#include <cstdlib>
+
 #include "lpc_common.cuh"
 
 LPC_DECLARE_STATUS(g_decode_status)
@@ -190,6 +192,9 @@ __global__ void __launch_bounds__((NCWARPS + 1) * 32)
   float* red = reinterpret_cast<float*>(smem + 2 * NSTAGE * SLAB + 2 * NSTAGE * 8);
   // red: [NCWARPS][G][D + 2]
 
+  // the combine kernel, launched with programmatic stream serialisation, may
+  // be scheduled now; it waits for this grid to complete before reading
+  lpc::pdl_trigger();
   const int split = blockIdx.x;
   const int kvh = blockIdx.y;
   const int64_t b = blockIdx.z;
@@ -376,6 +381,8 @@ __global__ void __launch_bounds__(COMBINE_WARPS * 32) decode_combine_kernel(
   // serialisation (the packed decode GEMM), may start its weight stream now;
   // it waits for this grid to complete before reading `out`
   lpc::pdl_trigger();
+  // launched under the split kernel: its partials are complete past here
+  lpc::pdl_wait();
   constexpr int DPL = D / 32;
   const int64_t bh = (int64_t)blockIdx.x * COMBINE_WARPS + (threadIdx.x >> 5);
   if (bh >= bh_total) return;
@@ -451,9 +458,27 @@ int launch_g(const void* q, const void* kc, const void* vc, const int32_t* lens,
       scale_log2, rows);
   if ((rc = lpc::check_launch("decode_attention (split)"))) return rc;
   const int64_t bh_total = B * (int64_t)H;
-  decode_combine_kernel<T, D>
-      <<<(unsigned)((bh_total + COMBINE_WARPS - 1) / COMBINE_WARPS), COMBINE_WARPS * 32, 0, s>>>(
-          po, pml, lens, (T*)out, H, max_splits, Smax, rows, bh_total);
+  // programmatic stream serialisation: the combine grid is scheduled while the
+  // split grid drains (it waits on it before reading), instead of after
+  static const bool pdl = [] {
+    const char* e = getenv("LPC_PDL");
+    return !(e && e[0] == '0');
+  }();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((bh_total + COMBINE_WARPS - 1) / COMBINE_WARPS));
+  cfg.blockDim = dim3(COMBINE_WARPS * 32);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, decode_combine_kernel<T, D>, (const float*)po, (const float*)pml,
+                         lens, (T*)out, H, max_splits, Smax, rows, bh_total) != cudaSuccess) {
+    lpc::set_error("decode_attention (combine): launch failed");
+    return LPC_ERR_CUDA;
+  }
   return lpc::check_launch("decode_attention (combine)");
 }
 
