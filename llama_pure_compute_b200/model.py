@@ -67,11 +67,13 @@ FUSED_QKV_MAX_TOKENS = 32
 # rows' re-reads cost more than the norm kernel (49.8 against 43.5 us).
 NORM_IN_GEMM_MAX_TOKENS = 64
 # Decode steps with at most this many tokens run o_proj and down_proj with the
-# residual add on packed copies of their weights (lpc_wsgemm).  Off by
-# default: faster than cuBLAS in isolation at 32 tokens (13.7 against
-# 14.9 us for o_proj, 22.2 against 25.0 for down_proj) but 2% slower per
-# decode step at 32 sequences (4.60 against 4.52 ms).
-PACKED_RESIDUAL_MAX_TOKENS = 0
+# residual add on packed copies of their weights (lpc_wsgemm): 13.3 against
+# 15.6 us (cuBLAS) for o_proj and 22.0 against 25.0 for down_proj at 32
+# tokens.  With the norms inside the packed GEMMs every kernel of the layer
+# after attention is a programmatic launch under the one before it: decode
+# step 4.35 against 4.46 ms at 32 sequences, 3.52 against 3.74 at 16; at 64
+# sequences it loses (6.07 against 5.90 ms).
+PACKED_RESIDUAL_MAX_TOKENS = 32
 
 __all__ = ["precompute_freqs_cis", "LlamaAttention", "LlamaDecodeLayer", "LlamaModel",
            "LlamaForCausalLM"]
