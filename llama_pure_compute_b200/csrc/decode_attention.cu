@@ -195,6 +195,8 @@ __global__ void __launch_bounds__((NCWARPS + 1) * 32)
   // the combine kernel, launched with programmatic stream serialisation, may
   // be scheduled now; it waits for this grid to complete before reading
   lpc::pdl_trigger();
+  // launched the same way under the kernel that wrote q and the new K/V rows
+  lpc::pdl_wait();
   const int split = blockIdx.x;
   const int kvh = blockIdx.y;
   const int64_t b = blockIdx.z;
@@ -452,26 +454,45 @@ int launch_g(const void* q, const void* kc, const void* vc, const int32_t* lens,
   static std::atomic<uint64_t> mask{0};
   int rc = lpc::once_per_device_smem((const void*)decode_split_kernel<T, D, G>, smem, mask);
   if (rc) return rc;
-  dim3 grid((unsigned)max_splits, (unsigned)Hkv, (unsigned)B);
-  decode_split_kernel<T, D, G><<<grid, (NCWARPS + 1) * 32, smem, s>>>(
-      (const T*)q, (const T*)kc, (const T*)vc, lens, (T*)out, po, pml, H, Hkv, Smax, max_splits,
-      scale_log2, rows);
-  if ((rc = lpc::check_launch("decode_attention (split)"))) return rc;
-  const int64_t bh_total = B * (int64_t)H;
-  // programmatic stream serialisation: the combine grid is scheduled while the
-  // split grid drains (it waits on it before reading), instead of after
+  // programmatic stream serialisation for both grids: each is scheduled while
+  // the grid before it drains, and waits on it before reading
   static const bool pdl = [] {
     const char* e = getenv("LPC_PDL");
     return !(e && e[0] == '0');
   }();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  {
+    // the split grid goes in early only while it is small: decode step 4.32
+    // against 4.35 ms at 32 sequences (3,072 CTAs), 15.00 against 14.97 at
+    // 256 (24,576 CTAs, whose first wave then competes with the tail of the
+    // kernel before it)
+    const int64_t ctas = (int64_t)max_splits * Hkv * B;
+    cudaLaunchAttribute sattr[1];
+    sattr[0] = attr[0];
+    sattr[0].val.programmaticStreamSerializationAllowed = pdl && ctas <= 4096 ? 1 : 0;
+    cudaLaunchConfig_t sc = {};
+    sc.gridDim = dim3((unsigned)max_splits, (unsigned)Hkv, (unsigned)B);
+    sc.blockDim = dim3((NCWARPS + 1) * 32);
+    sc.dynamicSmemBytes = (size_t)smem;
+    sc.stream = s;
+    sc.attrs = sattr;
+    sc.numAttrs = 1;
+    if (cudaLaunchKernelEx(&sc, decode_split_kernel<T, D, G>, (const T*)q, (const T*)kc,
+                           (const T*)vc, lens, (T*)out, po, pml, H, Hkv, Smax, max_splits,
+                           scale_log2, rows) != cudaSuccess) {
+      lpc::set_error("decode_attention (split): launch failed");
+      return LPC_ERR_CUDA;
+    }
+  }
+  if ((rc = lpc::check_launch("decode_attention (split)"))) return rc;
+  const int64_t bh_total = B * (int64_t)H;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((bh_total + COMBINE_WARPS - 1) / COMBINE_WARPS));
   cfg.blockDim = dim3(COMBINE_WARPS * 32);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, decode_combine_kernel<T, D>, (const float*)po, (const float*)pml,
