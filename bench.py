@@ -529,7 +529,7 @@ def _kentry(kernel, shape, us, *, nbytes=None, flops=None, hbm, tc, timing):
     return d
 
 
-KERNEL_KEYS = ("swiglu_pair", "wsgemm_swiglu", "wsgemm_qkv", "prefill", "swiglu_f32",
+KERNEL_KEYS = ("swiglu_pair", "wsgemm_swiglu", "wsgemm_qkv", "wsgemm_resid", "prefill", "swiglu_f32",
                "rope_kv_append", "kv_append", "rmsnorm", "decode")
 
 
@@ -583,12 +583,15 @@ def measure_kernels(dev, only=None):
                                nbytes=2 * I * D * 2 + M * D * 2 + M * I * 2,
                                flops=2 * M * D * 2 * I, hbm=hbm, tc=tc, timing=steady))
         if want("wsgemm_swiglu"):
-            # decode-sized SwiGLU on packed weights (32 tokens, normed input)
-            pws = [PackedWeight(w, layout="swiglu") for w in ws]
+            # decode-sized norm + SwiGLU on packed weights (32 tokens): the
+            # decode step's form, the norm weight folded into the packed copy
+            nw = 1 + 0.02 * rn(D)
+            pws = [PackedWeight(w, layout="swiglu", norm_weight=nw) for w in ws]
             M = 32
             x = rn(M, D)
-            us = _time_rotating([lambda pw=pw: packed_linear(x, pw, "swiglu") for pw in pws])
-            out.append(_kentry("wsgemm_kernel (SwiGLU epilogue)", "7B gate/up, 32 tokens",
+            us = _time_rotating([lambda pw=pw: packed_linear(x, pw, "swiglu", norm_eps=1e-5)
+                                 for pw in pws])
+            out.append(_kentry("wsgemm_kernel (norm + SwiGLU epilogue)", "7B gate/up, 32 tokens",
                                us, nbytes=2 * I * D * 2 + M * D * 2 + M * I * 2, hbm=hbm, tc=tc,
                                timing=steady))
             del pws
@@ -598,7 +601,8 @@ def measure_kernels(dev, only=None):
             # q/k/v projection + RoPE + KV append (32 tokens, normed input)
             M = 32
             wq = [rn(3 * H * 128, D, std=0.02) for _ in range(6)]
-            pq = [PackedWeight(w, layout="heads") for w in wq]
+            nq = 1 + 0.02 * rn(D)
+            pq = [PackedWeight(w, layout="heads", norm_weight=nq) for w in wq]
             cos, sin = precompute_freqs_cis(128, 1024, device=dev)
             cos, sin = cos.to(bf), sin.to(bf)
             x = rn(M, 1, D)
@@ -606,12 +610,26 @@ def measure_kernels(dev, only=None):
             kc = torch.zeros(M, H, 1024, 128, device=dev, dtype=bf)
             vc = torch.zeros_like(kc)
             us = _time_rotating([lambda pw=pw: ops.qkv_rope_append(x, pw, pos, cos, sin, kc, vc, H,
-                                                                   H) for pw in pq])
-            out.append(_kentry("wsgemm_kernel (EPI_QKV: projection + RoPE + KV append)",
+                                                                   H, norm_eps=1e-5) for pw in pq])
+            out.append(_kentry("wsgemm_kernel (EPI_QKV: norm + projection + RoPE + KV append)",
                                "7B q/k/v, 32 tokens", us,
                                nbytes=3 * H * 128 * D * 2 + M * D * 2 + M * 3 * H * 128 * 2,
                                hbm=hbm, tc=tc, timing=steady))
             del wq, pq, kc, vc
+        if want("wsgemm_resid"):
+            # o_proj and down_proj + residual on packed weights (32 tokens)
+            M = 32
+            po = [PackedWeight(rn(D, D, std=0.02)) for _ in range(12)]
+            pd = [PackedWeight(rn(D, I, std=0.02)) for _ in range(6)]
+            xo, xd, r = rn(M, D), rn(M, I), rn(M, D)
+            for name, pws, xin, kin in (("o_proj", po, xo, D), ("down_proj", pd, xd, I)):
+                us = _time_rotating([lambda pw=pw: packed_linear(xin, pw, "residual", resid=r, out=r)
+                                     for pw in pws])
+                out.append(_kentry("wsgemm_kernel (residual epilogue, split k)",
+                                   f"7B {name}, 32 tokens", us,
+                                   nbytes=D * kin * 2 + M * kin * 2 + 2 * M * D * 2, hbm=hbm, tc=tc,
+                                   timing=steady))
+            del po, pd
         if want("prefill"):
             # prefill attention [4, 32, 2048, 128] causal
             q, k, v = (rn(4, 32, 2048, 128) for _ in range(3))
