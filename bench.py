@@ -417,6 +417,7 @@ def run_ours(args, world, rank, local):
     except (OSError, ValueError):
         pass
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    read_peak = measure_read_peak(dev)
     # algorithmic bytes of one decode step: every weight once (the embedding
     # table only for the B gathered rows) + the KV cache at the timed steps'
     # mean context
@@ -480,7 +481,8 @@ def run_ours(args, world, rank, local):
                     "wall_ms": round(wall_e2e, 2)},
             "gpu_launches": launches_per_step * args.steps,
             "roofline": {
-                "kernel": "decode_split_kernel + decode_combine_kernel (split-KV decode attention)",
+                "kernel": "decode_split_kernel (+ decode_combine_kernel when a split does not "
+                          "cover the cache length): split-KV decode attention",
                 "bound": "hbm",
                 "achieved": round(attn_gbs, 1),
                 "peak": hbm_peak,
@@ -492,6 +494,11 @@ def run_ours(args, world, rank, local):
                 "algorithmic_bytes_per_launch": attn_bytes,
                 "launch_us": round(attn_us, 2),
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (burst)" if peaks else "fallback 6650",
+                "read_peak": round(read_peak, 1),
+                "frac_of_read_peak": round(attn_gbs / read_peak, 4),
+                "read_peak_source": "lpc_hbm_read_probe on 4 GiB in this run: a read-only stream "
+                                    "of 128 KB bulk-copy items (the peak above is a copy, which "
+                                    "moves every byte twice)",
             },
             "step_roofline": {
                 "bytes_per_step": step_bytes,
@@ -513,6 +520,26 @@ def run_ours(args, world, rank, local):
         raise SystemExit(3)
 
 
+def measure_read_peak(dev, nbytes: int = 4 << 30, reps: int = 10) -> float:
+    """HBM read ceiling in GB/s: lpc_hbm_read_probe over a buffer far larger
+    than L2, launched back to back and timed with CUDA events."""
+    lib = _lib.load()
+    buf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    for _ in range(3):
+        _lib.check(lib.lpc_hbm_read_probe(buf.data_ptr(), nbytes, st), "hbm_read_probe")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record()
+    for _ in range(reps):
+        lib.lpc_hbm_read_probe(buf.data_ptr(), nbytes, st)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    del buf
+    return nbytes / (us * 1e-6) / 1e9
+
+
 # ---------------------------------------------------------------------------
 # per-kernel rooflines in the decode line (same run, CUDA events)
 # ---------------------------------------------------------------------------
@@ -530,7 +557,7 @@ def _kentry(kernel, shape, us, *, nbytes=None, flops=None, hbm, tc, timing):
 
 
 KERNEL_KEYS = ("swiglu_pair", "wsgemm_swiglu", "wsgemm_qkv", "wsgemm_resid", "prefill", "swiglu_f32",
-               "rope_kv_append", "kv_append", "rmsnorm", "decode")
+               "rope_kv_append", "kv_append", "rmsnorm", "decode", "decode_b256")
 
 
 def measure_kernels(dev, only=None):
@@ -695,10 +722,30 @@ def measure_kernels(dev, only=None):
             wsd = ops.decode_attention_workspace(64, H, Smax, 128, dev)
             od = torch.empty_like(qd)
             us = _time_us(lambda: ops.decode_attention(qd, kc, vc, lens, None, od, wsd), 10)
-            out.append(_kentry("decode_split_kernel + decode_combine_kernel",
+            out.append(_kentry("decode_split_kernel + decode_combine_kernel (1024-key splits)",
                                "64 sequences, L ~ U[128, 4096], 32 heads x 128", us,
                                nbytes=int((L + 1).sum()) * H * 128 * 2 * 2 + 2 * 64 * H * 128 * 2,
                                hbm=hbm, tc=tc, timing="4.3 GB cache (> L2), launches back to back"))
+            del kc, vc
+    if want("decode_b256"):
+        with torch.inference_mode():
+            # one layer of the decode config: 256 sequences at context 576 in
+            # a 616-key cache (one 1024-key split per sequence and KV head:
+            # the split kernel alone, no combine launch)
+            B2, L2, Smax2 = 256, 576, 616
+            kc = rn(B2, H, Smax2, 128)
+            vc = rn(B2, H, Smax2, 128)
+            qd = rn(B2, H, 128)
+            lens = torch.full((B2,), L2, dtype=torch.int32, device=dev)
+            wsd = ops.decode_attention_workspace(B2, H, Smax2, 128, dev)
+            od = torch.empty_like(qd)
+            f = lambda: ops.decode_attention(qd, kc, vc, lens, None, od, wsd)  # noqa: E731
+            us = _time_rotating([f] * 10)
+            out.append(_kentry("decode_split_kernel",
+                               "256 sequences at 576 keys, 32 heads x 128 (one layer of the decode config)",
+                               us, nbytes=B2 * L2 * H * 128 * 2 * 2 + 2 * B2 * H * 128 * 2,
+                               hbm=hbm, tc=tc, timing="2.4 GB of K/V (> L2); 10 launches back to back "
+                                                        "behind a GPU sleep, best of 5"))
             del kc, vc
     torch.cuda.synchronize()
     torch.cuda.empty_cache()

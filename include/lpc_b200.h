@@ -182,10 +182,22 @@ LPC_API int lpc_rmsswiglu_folded_forward(const void* x, const void* gate_w, cons
  * seq_lens: int32 [batch] on the device, keys [0, seq_lens[b]) are attended;
  * out: [batch, heads, head_dim].  head_dim 32, 64 or 128; bf16 or fp16.
  * workspace: lpc_decode_attention_workspace_bytes(batch, heads, max_seq_len, head_dim)
- * bytes (per-split partial results).
+ * bytes (per-split partial results).  Each sequence is cut into splits of
+ * lpc_decode_attention_split_keys(batch, kv_heads, max_seq_len) keys, one CTA
+ * each; a second (combine) kernel merges them unless that length is at least
+ * max_seq_len.
  */
 LPC_API int64_t lpc_decode_attention_workspace_bytes(int64_t batch, int heads, int64_t max_seq_len,
                                              int head_dim);
+
+/* Keys per split that the decode attention calls use for `batch` sequences,
+ * `kv_heads` KV heads and a cache of max_seq_len keys per sequence: 1024 with
+ * at least 2048 (sequence, KV head) pairs; 512 with a cache of >= 2048 keys
+ * whose 512-key splits still give 2048 CTAs; else 256 (the environment
+ * variable LPC_DECODE_CHUNK, a multiple of 32 in [256, 65536], overrides
+ * it).  The calls launch one kernel when the result is >= max_seq_len, two
+ * otherwise.  0 for invalid sizes.  Host only. */
+LPC_API int lpc_decode_attention_split_keys(int64_t batch, int kv_heads, int64_t max_seq_len);
 LPC_API int lpc_decode_attention(const void* q, const void* key_cache, const void* value_cache,
                          const int32_t* seq_lens, void* out, void* workspace,
                          int64_t workspace_bytes, int64_t batch, int heads, int kv_heads,
@@ -340,6 +352,16 @@ LPC_API int lpc_qkv_rope_append(const void* x, const void* packed_w, const int64
                                 int num_kv_heads, int head_dim, int k, int64_t max_batch,
                                 int64_t max_seq_len, int64_t total_rows, int dtype, int table_dtype,
                                 float norm_eps, void* stream);
+
+/*
+ * HBM read-rate probe (a measurement utility; no reference counterpart).
+ * Reads `bytes` (a positive multiple of 131072) of `buf` the way the decode
+ * attention reads its cache rows: one CTA per 128 KB, 16 KB 1-D bulk copies
+ * into a 4-stage shared-memory ring, no arithmetic.  Bytes over its event
+ * time are the read ceiling of such a kernel; the copy rate usually quoted
+ * as peak counts every byte twice (read and write) and is lower.
+ */
+LPC_API int lpc_hbm_read_probe(const void* buf, int64_t bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -46,6 +46,7 @@ SIGNATURES = {
                                  _I, _P]),
     "lpc_rmsswiglu_folded_forward": (_I, [_P, _P, _P, _P, _I64, _I, _I, _F, _I, _P]),
     "lpc_decode_attention_workspace_bytes": (_I64, [_I64, _I, _I64, _I]),
+    "lpc_decode_attention_split_keys": (_I, [_I64, _I, _I64]),
     "lpc_decode_attention": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _I64, _I64, _F,
                                   _I, _P]),
     "lpc_decode_attention_noalloc": (_I, [_P, _P, _P, _P, _P, _I64, _I, _I, _I, _I64, _I64, _F, _I,
@@ -59,6 +60,7 @@ SIGNATURES = {
     "lpc_wsgemm": (_I, [_P, _P, _P, _P, _I64, _I64, _I, _I, _I, _F, _P]),
     "lpc_qkv_rope_append": (_I, [_P, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I, _I,
                                  _I, _I, _I64, _I64, _I64, _I, _I, _F, _P]),
+    "lpc_hbm_read_probe": (_I, [_P, _I64, _P]),
 }
 
 _lib = None
@@ -70,9 +72,19 @@ KERNELS_PER_CALL = {
     "lpc_rmsnorm_forward": 1, "lpc_rmsswiglu_forward": 2, "lpc_flash_attention": 1,
     "lpc_decode_attention": 2, "lpc_decode_attention_noalloc": 2,
     "lpc_pack_weights": 1, "lpc_wsgemm": 1, "lpc_qkv_rope_append": 1, "lpc_rope_kv_append_ragged": 1,
-    "lpc_decode_attention_ragged": 2, "lpc_rmsswiglu_folded_forward": 1,
+    "lpc_decode_attention_ragged": 2, "lpc_rmsswiglu_folded_forward": 1, "lpc_hbm_read_probe": 1,
 }
 launch_count = 0
+
+
+def decode_kernels(batch: int, kv_heads: int, max_seq_len: int) -> int:
+    """Kernels one decode-attention call enqueues: none for an empty batch,
+    the split kernel alone when one split covers the cache length, else the
+    split and combine kernels."""
+    if batch <= 0:
+        return 0
+    keys = load().lpc_decode_attention_split_keys(batch, kv_heads, max_seq_len)
+    return 1 if keys >= max_seq_len else 2
 
 
 def count_launch(name: str, n: int | None = None) -> None:

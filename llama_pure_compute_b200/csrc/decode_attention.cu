@@ -10,8 +10,10 @@
 //
 // Decomposition (HBM-streaming, no tensor cores: one query row per KV head
 // gives an arithmetic intensity of ~1 FLOP/byte):
-//   grid (split, kv_head, batch); each CTA owns CHUNK keys of one (b, kv head)
-//   and all G = heads/kv_heads query heads that share them.
+//   grid (split, kv_head, batch); each CTA owns one split of one (b, kv head)
+//   and all G = heads/kv_heads query heads that share them.  The host picks
+//   the split length `chunk` per launch (split_chunk): a sequence of L keys
+//   takes ceil(L / chunk) splits, the last one holding the remainder.
 //   warp 4     producer: cp.async.bulk copies of contiguous 32-key K and V
 //              slabs (8 KB each for head_dim 128 bf16) into a 4-stage ring,
 //              completion on mbarriers (tx bytes).
@@ -24,7 +26,8 @@
 //   CTA end    the 4 warps' (max, sum, acc) merge through shared memory; a
 //              sequence with a single split writes its output directly, else
 //              the split's partial goes to the workspace and a small combine
-//              kernel merges the splits.
+//              kernel merges the splits.  When every sequence fits one split
+//              (chunk >= max_seq_len) the combine kernel is not launched.
 #include <atomic>
 
 #include <cstdlib>
@@ -47,7 +50,7 @@ namespace {
 
 using lpc::Num;
 
-constexpr int CHUNK = 256;   // keys per split
+constexpr int CHUNK = 256;   // workspace granularity: the shortest split length
 constexpr int TILE = 32;     // keys per pipeline stage
 constexpr int NSTAGE = 4;
 constexpr int NCWARPS = 4;   // compute warps
@@ -181,7 +184,7 @@ __global__ void __launch_bounds__((NCWARPS + 1) * 32)
                         const T* __restrict__ vc, const int32_t* __restrict__ seq_lens,
                         T* __restrict__ out, float* __restrict__ part_o,
                         float* __restrict__ part_ml, int H, int Hkv, int64_t Smax,
-                        int max_splits, float scale_log2, KvRows rows) {
+                        int max_splits, int chunk, float scale_log2, KvRows rows) {
   constexpr int DPL = D / 32;                    // dims per lane
   constexpr int ROW_BYTES = D * (int)sizeof(T);
   constexpr int SLAB = TILE * ROW_BYTES;         // one K or V stage
@@ -202,11 +205,17 @@ __global__ void __launch_bounds__((NCWARPS + 1) * 32)
   const int64_t b = blockIdx.z;
   int64_t row0;  // cache row of (b, kv head, position 0)
   int L = rows.length(b, kvh, Hkv, Smax, __ldg(seq_lens + b), &row0, split == 0 && threadIdx.x == 0);
-  const int start = split * CHUNK;
-  if (start >= L) return;  // uniform for the whole CTA, before any barrier
-  const int end = min(start + CHUNK, L);
+  const int nsplits = L > 0 ? (L + chunk - 1) / chunk : 0;
+  if (split >= nsplits) {  // uniform for the whole CTA, before any barrier
+    // an empty context attends to nothing: its heads' outputs are zero
+    if (L <= 0 && split == 0)
+      for (int i = threadIdx.x; i < G * D; i += blockDim.x)
+        out[(b * H + (int64_t)kvh * G) * D + i] = Num<T>::from_f(0.f);
+    return;
+  }
+  const int start = split * chunk;
+  const int end = min(start + chunk, L);
   const int ntiles = (end - start + TILE - 1) / TILE;
-  const int nsplits = (L + CHUNK - 1) / CHUNK;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   auto full_bar = [&](int s) { return lpc::smem_u32(bar + s); };
@@ -378,7 +387,7 @@ template <typename T, int D>
 __global__ void __launch_bounds__(COMBINE_WARPS * 32) decode_combine_kernel(
     const float* __restrict__ part_o, const float* __restrict__ part_ml,
     const int32_t* __restrict__ seq_lens, T* __restrict__ out, int H, int max_splits,
-    int64_t Smax, KvRows rows, int64_t bh_total) {
+    int chunk, int64_t Smax, KvRows rows, int64_t bh_total) {
   // the projection after attention, when launched with programmatic stream
   // serialisation (the packed decode GEMM), may start its weight stream now;
   // it waits for this grid to complete before reading `out`
@@ -398,7 +407,7 @@ __global__ void __launch_bounds__(COMBINE_WARPS * 32) decode_combine_kernel(
     for (int i = 0; i < DPL; ++i) o[i] = Num<T>::from_f(0.f);
     return;
   }
-  const int ns = (L + CHUNK - 1) / CHUNK;
+  const int ns = (L + chunk - 1) / chunk;
   if (ns <= 1) return;  // written by the split kernel
   const float* ml = part_ml + bh * max_splits * 2;
   const float* po = part_o + bh * max_splits * D + lane * DPL;
@@ -448,7 +457,7 @@ __global__ void __launch_bounds__(COMBINE_WARPS * 32) decode_combine_kernel(
 template <typename T, int D, int G>
 int launch_g(const void* q, const void* kc, const void* vc, const int32_t* lens, void* out,
              float* po, float* pml, int64_t B, int H, int Hkv, int64_t Smax, int max_splits,
-             float scale_log2, const KvRows& rows, cudaStream_t s) {
+             int chunk, float scale_log2, const KvRows& rows, cudaStream_t s) {
   constexpr int SLAB = TILE * D * 2;
   const int smem = 2 * NSTAGE * SLAB + 2 * NSTAGE * 8 + NCWARPS * G * (D + 2) * 4;
   static std::atomic<uint64_t> mask{0};
@@ -463,17 +472,20 @@ int launch_g(const void* q, const void* kc, const void* vc, const int32_t* lens,
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  // splits a sequence of the cache's full length needs; shorter ones leave
+  // the trailing CTAs of their row idle
+  const int grid_splits = (int)((Smax + chunk - 1) / chunk);
   {
     // the split grid goes in early only while it is small: decode step 4.32
     // against 4.35 ms at 32 sequences (3,072 CTAs), 15.00 against 14.97 at
     // 256 (24,576 CTAs, whose first wave then competes with the tail of the
     // kernel before it)
-    const int64_t ctas = (int64_t)max_splits * Hkv * B;
+    const int64_t ctas = (int64_t)grid_splits * Hkv * B;
     cudaLaunchAttribute sattr[1];
     sattr[0] = attr[0];
     sattr[0].val.programmaticStreamSerializationAllowed = pdl && ctas <= 4096 ? 1 : 0;
     cudaLaunchConfig_t sc = {};
-    sc.gridDim = dim3((unsigned)max_splits, (unsigned)Hkv, (unsigned)B);
+    sc.gridDim = dim3((unsigned)grid_splits, (unsigned)Hkv, (unsigned)B);
     sc.blockDim = dim3((NCWARPS + 1) * 32);
     sc.dynamicSmemBytes = (size_t)smem;
     sc.stream = s;
@@ -481,12 +493,13 @@ int launch_g(const void* q, const void* kc, const void* vc, const int32_t* lens,
     sc.numAttrs = 1;
     if (cudaLaunchKernelEx(&sc, decode_split_kernel<T, D, G>, (const T*)q, (const T*)kc,
                            (const T*)vc, lens, (T*)out, po, pml, H, Hkv, Smax, max_splits,
-                           scale_log2, rows) != cudaSuccess) {
+                           chunk, scale_log2, rows) != cudaSuccess) {
       lpc::set_error("decode_attention (split): launch failed");
       return LPC_ERR_CUDA;
     }
   }
   if ((rc = lpc::check_launch("decode_attention (split)"))) return rc;
+  if (grid_splits == 1) return LPC_OK;  // every sequence was written by its single split
   const int64_t bh_total = B * (int64_t)H;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((bh_total + COMBINE_WARPS - 1) / COMBINE_WARPS));
@@ -496,7 +509,7 @@ int launch_g(const void* q, const void* kc, const void* vc, const int32_t* lens,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, decode_combine_kernel<T, D>, (const float*)po, (const float*)pml,
-                         lens, (T*)out, H, max_splits, Smax, rows, bh_total) != cudaSuccess) {
+                         lens, (T*)out, H, max_splits, chunk, Smax, rows, bh_total) != cudaSuccess) {
     lpc::set_error("decode_attention (combine): launch failed");
     return LPC_ERR_CUDA;
   }
@@ -506,12 +519,12 @@ int launch_g(const void* q, const void* kc, const void* vc, const int32_t* lens,
 template <typename T, int D>
 int launch_d(int G, const void* q, const void* kc, const void* vc, const int32_t* lens,
              void* out, float* po, float* pml, int64_t B, int H, int Hkv, int64_t Smax,
-             int max_splits, float sl2, const KvRows& r, cudaStream_t s) {
+             int max_splits, int ch, float sl2, const KvRows& r, cudaStream_t s) {
   switch (G) {
-    case 1: return launch_g<T, D, 1>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, sl2, r, s);
-    case 2: return launch_g<T, D, 2>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, sl2, r, s);
-    case 4: return launch_g<T, D, 4>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, sl2, r, s);
-    case 8: return launch_g<T, D, 8>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, sl2, r, s);
+    case 1: return launch_g<T, D, 1>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, ch, sl2, r, s);
+    case 2: return launch_g<T, D, 2>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, ch, sl2, r, s);
+    case 4: return launch_g<T, D, 4>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, ch, sl2, r, s);
+    case 8: return launch_g<T, D, 8>(q, kc, vc, lens, out, po, pml, B, H, Hkv, Smax, max_splits, ch, sl2, r, s);
   }
   lpc::set_error("decode_attention: heads/kv_heads = %d not supported (1, 2, 4 or 8)", G);
   return LPC_ERR_UNSUPPORTED;
@@ -534,6 +547,45 @@ extern "C" int64_t lpc_decode_attention_workspace_bytes(int64_t batch, int heads
     return 0;
   const int64_t max_splits = (max_seq_len + CHUNK - 1) / CHUNK;
   return batch * heads * max_splits * (int64_t)(head_dim + 2) * 4;
+}
+
+namespace {
+
+// Split length for one launch.  Longer splits cost fewer CTA start-ups and
+// partials, but the grid must stay several waves deep (about 440 CTAs run at
+// once: three per SM).  With `pairs` (sequence, KV head) pairs:
+//   * 1024 keys when pairs >= MIN_SPLIT_CTAS: a grid of one or more CTAs per
+//     pair is already deep enough;
+//   * 512 keys when the cache holds at least 2048 keys per sequence and the
+//     grid still has MIN_SPLIT_CTAS CTAs for a full-length context;
+//   * 256 keys otherwise.
+// Measured on the 7B decode shape (32 KV heads, head_dim 128, us per call):
+// every sequence at 576 keys, 256 / 128 / 64 sequences 336 / 172 / 90 with
+// 1024-key splits against 348 / 179 / 95 with 256-key ones, 32 and 16
+// sequences 50.6 / 29.5 with 256 against 52.4 / 31.7 with two or three
+// equal splits; 8 sequences of 4096 keys 84.6 with 512 against 87.5 with 256.
+// LPC_DECODE_CHUNK=<keys> (a multiple of 32 from 256 to 65536) overrides the
+// choice.
+constexpr int64_t MIN_SPLIT_CTAS = 2048;
+int split_chunk(int64_t pairs, int64_t max_seq_len) {
+  static const int forced = [] {
+    const char* e = getenv("LPC_DECODE_CHUNK");
+    const int v = e ? atoi(e) : 0;
+    return (v >= CHUNK && v <= 65536 && v % TILE == 0) ? v : 0;
+  }();
+  if (forced) return forced;
+  if (pairs >= MIN_SPLIT_CTAS) return 1024;
+  if (max_seq_len >= 2048 && pairs * ((max_seq_len + 511) / 512) >= MIN_SPLIT_CTAS) return 512;
+  return CHUNK;
+}
+
+}  // namespace
+
+extern "C" int lpc_decode_attention_split_keys(int64_t batch, int kv_heads, int64_t max_seq_len) {
+  if (batch <= 0 || kv_heads <= 0 || max_seq_len <= 0 || batch > MAX_DECODE_BATCH ||
+      kv_heads > MAX_DECODE_HEADS || max_seq_len > MAX_DECODE_SEQ)
+    return 0;
+  return split_chunk(batch * kv_heads, max_seq_len);
 }
 
 namespace {
@@ -582,18 +634,19 @@ int decode_common(const void* q, const void* key_cache, const void* value_cache,
   const int G = heads / kv_heads;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int ms = (int)max_splits;
+  const int ch = split_chunk(batch * kv_heads, max_seq_len);
   if (dtype == LPC_DTYPE_BF16) {
     if (head_dim == 128)
-      return launch_d<__nv_bfloat16, 128>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
+      return launch_d<__nv_bfloat16, 128>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, ch, sl2, rows, s);
     if (head_dim == 64)
-      return launch_d<__nv_bfloat16, 64>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
-    return launch_d<__nv_bfloat16, 32>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
+      return launch_d<__nv_bfloat16, 64>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, ch, sl2, rows, s);
+    return launch_d<__nv_bfloat16, 32>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, ch, sl2, rows, s);
   }
   if (head_dim == 128)
-    return launch_d<__half, 128>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
+    return launch_d<__half, 128>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, ch, sl2, rows, s);
   if (head_dim == 64)
-    return launch_d<__half, 64>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
-  return launch_d<__half, 32>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, sl2, rows, s);
+    return launch_d<__half, 64>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, ch, sl2, rows, s);
+  return launch_d<__half, 32>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, ch, sl2, rows, s);
 }
 
 }  // namespace

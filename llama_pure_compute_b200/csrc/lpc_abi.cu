@@ -154,6 +154,7 @@ unsigned int lpc_status_decode(bool clear);
 unsigned int lpc_status_swiglu(bool clear);
 unsigned int lpc_status_prefill(bool clear);
 unsigned int lpc_status_wsgemm(bool clear);
+unsigned int lpc_status_probe(bool clear);
 
 extern "C" int lpc_version(void) { return 100; }
 
@@ -165,6 +166,7 @@ extern "C" int lpc_device_status(void) {
     return -1;
   }
   unsigned int s = lpc_status_kv(true) | lpc_status_rope(true) | lpc_status_decode(true) |
-                   lpc_status_swiglu(true) | lpc_status_prefill(true) | lpc_status_wsgemm(true);
+                   lpc_status_swiglu(true) | lpc_status_prefill(true) | lpc_status_wsgemm(true) |
+                   lpc_status_probe(true);
   return static_cast<int>(s);
 }

@@ -369,7 +369,7 @@ def decode_attention(
         out.data_ptr(), workspace.data_ptr(), workspace.numel(), B, H, Hkv, D, Bmax, Smax,
         float(sm_scale), _lib.dtype_code(q.dtype, "decode_attention"), _lib.stream_of(q))
     _lib.check(rc, "decode_attention")
-    _lib.count_launch("lpc_decode_attention")
+    _lib.count_launch("lpc_decode_attention", _lib.decode_kernels(B, Hkv, Smax))
     return out
 
 
@@ -552,5 +552,5 @@ def decode_attention_ragged(
         workspace.numel(), B, H, Hkv, D, total_rows, max_seq_len, float(sm_scale),
         _lib.dtype_code(q.dtype, "decode_attention_ragged"), _lib.stream_of(q))
     _lib.check(rc, "decode_attention_ragged")
-    _lib.count_launch("lpc_decode_attention_ragged")
+    _lib.count_launch("lpc_decode_attention_ragged", _lib.decode_kernels(B, Hkv, max_seq_len))
     return out

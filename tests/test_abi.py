@@ -87,6 +87,30 @@ def test_workspace_queries():
     assert n == 64 * 32 * 17 * 130 * 4
 
 
+def test_decode_split_keys_rule():
+    """The split length decode attention picks from its grid (host only):
+    1024 keys from 2048 (sequence, KV head) pairs up, 512 for long caches
+    whose 512-key splits still give 2048 CTAs, else 256; the launch count
+    follows (one kernel when a split covers the cache length)."""
+    lib = _lib.load()
+    sk = lib.lpc_decode_attention_split_keys
+    assert sk(256, 32, 600) == 1024 and sk(64, 32, 600) == 1024      # 8192 / 2048 pairs
+    assert sk(32, 32, 600) == 256 and sk(16, 32, 616) == 256          # 1024 / 512 pairs
+    assert sk(32, 32, 1064) == 256                                    # cache below 2048 keys
+    assert sk(8, 32, 4096) == 512 and sk(16, 32, 8192) == 512         # 256 x 8, 512 x 16 CTAs
+    assert sk(1, 32, 4096) == 256                                     # 32 x 8 < 2048
+    assert sk(0, 32, 600) == 0 and sk(4, 0, 600) == 0 and sk(4, 32, 0) == 0
+    assert _lib.decode_kernels(256, 32, 600) == 1 and _lib.decode_kernels(256, 32, 1025) == 2
+    assert _lib.decode_kernels(32, 32, 600) == 2 and _lib.decode_kernels(0, 32, 600) == 0
+
+
+def test_read_probe_validates_on_the_host():
+    lib = _lib.load()
+    assert lib.lpc_hbm_read_probe(None, 131072, None) == _lib.LPC_ERR_INVALID
+    assert lib.lpc_hbm_read_probe(16, 1000, None) == _lib.LPC_ERR_INVALID
+    assert b"multiple of 131072" in lib.lpc_last_error()
+
+
 def test_decode_sizes_that_would_overflow_are_rejected_on_the_host():
     """Sizes beyond the split grid (65535 splits of 256 keys, 65535 sequences)
     are refused before any size arithmetic: no wrapped, negative workspace

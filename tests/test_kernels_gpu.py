@@ -576,3 +576,30 @@ def test_decode_independent_of_workspace_contents(H, Hkv):
                                D ** -0.5)
     assert (o1.float().cpu() - ref).abs().max().item() <= 2e-2
     assert o1[1].abs().sum().item() == 0
+
+
+@pytest.mark.parametrize("B,Smax,lens", [
+    # 64 x 32 (sequence, KV head) pairs, a cache of <= 1024 keys: one split
+    # of up to 1024 keys per sequence, no combine launch
+    (64, 1000, [1000, 0, 1, 31, 32, 33, 500, 999]),
+    # 8 x 32 pairs, a 4096-key cache: 512-key splits
+    (8, 4096, [4096, 4095, 513, 512, 511, 1, 0, 2000]),
+])
+def test_decode_split_lengths(B, Smax, lens):
+    """The split length each launch picks from its grid (1024, 512 or 256
+    keys): outputs against the oracle at lengths around the split and tile
+    edges, zeros for an empty context (written by the split kernel when no
+    combine kernel runs), the device status clean."""
+    H = Hkv = 32
+    D = 128
+    g = torch.Generator(device=DEV).manual_seed(B)
+    L = torch.tensor((lens * (B // len(lens) + 1))[:B], dtype=torch.int32)
+    kc = torch.randn(B, Hkv, Smax, D, device=DEV, generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, Hkv, Smax, D, device=DEV, generator=g).to(torch.bfloat16)
+    q = torch.randn(B, H, D, device=DEV, generator=g).to(torch.bfloat16)
+    o = ops.decode_attention(q, kc, vc, L.to(DEV)).float().cpu()
+    ref = decode_attention_ref(q.float().cpu(), kc.float().cpu(), vc.float().cpu(), L,
+                               D ** -0.5).float()
+    assert (o - ref).abs().max().item() <= 2e-2
+    assert o[L == 0].abs().sum().item() == 0
+    assert _lib.device_status() == 0
