@@ -523,6 +523,7 @@ def run_ours(args, world, rank, local):
 def measure_read_peak(dev, nbytes: int = 4 << 30, reps: int = 10) -> float:
     """HBM read ceiling in GB/s: lpc_hbm_read_probe over a buffer far larger
     than L2, launched back to back and timed with CUDA events."""
+    from llama_pure_compute_b200 import _lib
     lib = _lib.load()
     buf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     st = torch.cuda.current_stream(dev).cuda_stream

@@ -110,36 +110,52 @@ __device__ __forceinline__ float unpack1<__half>(uint32_t w) {
   return __half2float(__ushort_as_half((unsigned short)w));
 }
 
-// q . k over this lane's DPL dims (fixed order).
+// Packed fp32 pairs: Blackwell's f32x2 FMA does two lanes of work in one
+// instruction (even dims in the low half, odd dims in the high half).
+__device__ __forceinline__ uint64_t pack_f2(float lo, float hi) {
+  return ((uint64_t)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t fma_f2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+template <typename T>
+__device__ __forceinline__ uint64_t unpack_f2(uint32_t w) {
+  float a, c;
+  unpack2<T>(w, a, c);
+  return pack_f2(a, c);
+}
+
+// q . k over this lane's DPL dims: even and odd dims accumulate in the two
+// halves of an f32x2 FMA chain (fixed order), then one add.
 template <typename T, int DPL>
 __device__ __forceinline__ float row_dot(const RawRow<DPL>& r, const float* qf) {
   if constexpr (DPL == 1) {
     return qf[0] * unpack1<T>(r.w[0]);
   } else {
-    float acc_d = 0.f;
+    uint64_t s = 0ull;  // +0.0f in both halves
 #pragma unroll
-    for (int w = 0; w < DPL / 2; ++w) {
-      float a, c;
-      unpack2<T>(r.w[w], a, c);
-      acc_d = fmaf(qf[2 * w], a, acc_d);
-      acc_d = fmaf(qf[2 * w + 1], c, acc_d);
-    }
-    return acc_d;
+    for (int w = 0; w < DPL / 2; ++w)
+      s = fma_f2(pack_f2(qf[2 * w], qf[2 * w + 1]), unpack_f2<T>(r.w[w]), s);
+    return lo_f(s) + hi_f(s);
   }
 }
 
-// acc += p * v over this lane's DPL dims.
+// acc += p * v over this lane's DPL dims (f32x2 FMAs, one per pair of dims).
 template <typename T, int DPL>
 __device__ __forceinline__ void row_axpy(const RawRow<DPL>& r, float p, float* acc) {
   if constexpr (DPL == 1) {
     acc[0] = fmaf(p, unpack1<T>(r.w[0]), acc[0]);
   } else {
+    const uint64_t pp = pack_f2(p, p);
 #pragma unroll
     for (int w = 0; w < DPL / 2; ++w) {
-      float a, c;
-      unpack2<T>(r.w[w], a, c);
-      acc[2 * w] = fmaf(p, a, acc[2 * w]);
-      acc[2 * w + 1] = fmaf(p, c, acc[2 * w + 1]);
+      const uint64_t d = fma_f2(pp, unpack_f2<T>(r.w[w]), pack_f2(acc[2 * w], acc[2 * w + 1]));
+      acc[2 * w] = lo_f(d);
+      acc[2 * w + 1] = hi_f(d);
     }
   }
 }
