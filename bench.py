@@ -45,10 +45,11 @@ PROMPT_LEN = 512
 NEW_TOKENS = 128
 SEED = 3
 # ncu dram bytes (read + write) / algorithmic bytes of the decode-attention
-# kernel, from one dram__bytes capture of a 16-sequence ragged launch (589.1 MB
-# of traffic for 583.9 MB of K/V, q and output).  The bench scales it to its
-# own launch (traffic grows with the K/V bytes processed).
-DECODE_ATTN_TRAFFIC_RATIO = (583.322880e6 + 5.812224e6) / 583.942144e6
+# kernel, from one full capture of the split kernel on one layer of the decode
+# config (256 sequences at 576 keys: 2,418.0 MB read + 6.0 MB written for
+# 2,420.1 MB of K/V, q and output).  The bench scales it to its own launch
+# (traffic grows with the K/V bytes processed).
+DECODE_ATTN_TRAFFIC_RATIO = (2418.039e6 + 5.953536e6) / 2420.113408e6
 
 
 def parse():
@@ -489,8 +490,9 @@ def run_ours(args, world, rank, local):
                 "unit": "GB/s",
                 "frac": round(attn_gbs / hbm_peak, 4),
                 "traffic": int(attn_bytes * DECODE_ATTN_TRAFFIC_RATIO),
-                "traffic_source": "ncu dram__bytes of a 16-sequence ragged decode-attention "
-                                  "launch, scaled by the K/V bytes of this launch",
+                "traffic_source": "ncu dram__bytes of the split kernel on one layer of this "
+                                  "workload (256 sequences at 576 keys), scaled by the K/V "
+                                  "bytes of this launch",
                 "algorithmic_bytes_per_launch": attn_bytes,
                 "launch_us": round(attn_us, 2),
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (burst)" if peaks else "fallback 6650",
