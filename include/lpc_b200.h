@@ -183,21 +183,24 @@ LPC_API int lpc_rmsswiglu_folded_forward(const void* x, const void* gate_w, cons
  * out: [batch, heads, head_dim].  head_dim 32, 64 or 128; bf16 or fp16.
  * workspace: lpc_decode_attention_workspace_bytes(batch, heads, max_seq_len, head_dim)
  * bytes (per-split partial results).  Each sequence is cut into splits of
- * lpc_decode_attention_split_keys(batch, kv_heads, max_seq_len) keys, one CTA
- * each; a second (combine) kernel merges them unless that length is at least
- * max_seq_len.
+ * lpc_decode_attention_split_keys(batch, kv_heads, max_seq_len, 0) keys (the
+ * ragged call: its total_rows instead of 0), one CTA each; a second (combine)
+ * kernel merges them unless that length is at least max_seq_len.
  */
 LPC_API int64_t lpc_decode_attention_workspace_bytes(int64_t batch, int heads, int64_t max_seq_len,
                                              int head_dim);
 
 /* Keys per split that the decode attention calls use for `batch` sequences,
- * `kv_heads` KV heads and a cache of max_seq_len keys per sequence: 1024 with
- * at least 2048 (sequence, KV head) pairs; 512 with a cache of >= 2048 keys
- * whose 512-key splits still give 2048 CTAs; else 256 (the environment
- * variable LPC_DECODE_CHUNK, a multiple of 32 in [256, 65536], overrides
- * it).  The calls launch one kernel when the result is >= max_seq_len, two
- * otherwise.  0 for invalid sizes.  Host only. */
-LPC_API int lpc_decode_attention_split_keys(int64_t batch, int kv_heads, int64_t max_seq_len);
+ * `kv_heads` KV heads and a cache of max_seq_len keys per sequence
+ * (total_rows: the ragged cache's rows per KV head; <= 0 for the dense
+ * cache, whose capacity is batch * max_seq_len).  1024 with at least 2048
+ * (sequence, KV head) pairs, or when whole 1024-key splits of the capacity
+ * give 2048 CTAs; 512 when whole 512-key splits do; else 256.  The
+ * environment variable LPC_DECODE_CHUNK (a multiple of 32 in [256, 65536])
+ * overrides it.  The calls launch one kernel when the result is >=
+ * max_seq_len, two otherwise.  0 for invalid sizes.  Host only. */
+LPC_API int lpc_decode_attention_split_keys(int64_t batch, int kv_heads, int64_t max_seq_len,
+                                            int64_t total_rows);
 LPC_API int lpc_decode_attention(const void* q, const void* key_cache, const void* value_cache,
                          const int32_t* seq_lens, void* out, void* workspace,
                          int64_t workspace_bytes, int64_t batch, int heads, int kv_heads,

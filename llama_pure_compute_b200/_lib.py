@@ -46,7 +46,7 @@ SIGNATURES = {
                                  _I, _P]),
     "lpc_rmsswiglu_folded_forward": (_I, [_P, _P, _P, _P, _I64, _I, _I, _F, _I, _P]),
     "lpc_decode_attention_workspace_bytes": (_I64, [_I64, _I, _I64, _I]),
-    "lpc_decode_attention_split_keys": (_I, [_I64, _I, _I64]),
+    "lpc_decode_attention_split_keys": (_I, [_I64, _I, _I64, _I64]),
     "lpc_decode_attention": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I, _I64, _I64, _F,
                                   _I, _P]),
     "lpc_decode_attention_noalloc": (_I, [_P, _P, _P, _P, _P, _I64, _I, _I, _I, _I64, _I64, _F, _I,
@@ -77,13 +77,14 @@ KERNELS_PER_CALL = {
 launch_count = 0
 
 
-def decode_kernels(batch: int, kv_heads: int, max_seq_len: int) -> int:
+def decode_kernels(batch: int, kv_heads: int, max_seq_len: int, total_rows: int = 0) -> int:
     """Kernels one decode-attention call enqueues: none for an empty batch,
     the split kernel alone when one split covers the cache length, else the
-    split and combine kernels."""
+    split and combine kernels (total_rows: the ragged cache's rows per KV
+    head, 0 for the dense cache)."""
     if batch <= 0:
         return 0
-    keys = load().lpc_decode_attention_split_keys(batch, kv_heads, max_seq_len)
+    keys = load().lpc_decode_attention_split_keys(batch, kv_heads, max_seq_len, total_rows)
     return 1 if keys >= max_seq_len else 2
 
 

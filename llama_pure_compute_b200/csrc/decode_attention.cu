@@ -569,39 +569,43 @@ namespace {
 
 // Split length for one launch.  Longer splits cost fewer CTA start-ups and
 // partials, but the grid must stay several waves deep (about 440 CTAs run at
-// once: three per SM).  With `pairs` (sequence, KV head) pairs:
-//   * 1024 keys when pairs >= MIN_SPLIT_CTAS: a grid of one or more CTAs per
-//     pair is already deep enough;
-//   * 512 keys when the cache holds at least 2048 keys per sequence and the
-//     grid still has MIN_SPLIT_CTAS CTAs for a full-length context;
+// once: three per SM).  `total_keys` is the cache capacity over all
+// sequences (dense: batch * max_seq_len; ragged: the rows per KV head):
+//   * 1024 keys when there are at least MIN_SPLIT_CTAS (sequence, KV head)
+//     pairs (one or more CTAs per pair is already a deep grid), or when full
+//     1024-key splits of the capacity give MIN_SPLIT_CTAS CTAs;
+//   * 512 keys when full 512-key splits give MIN_SPLIT_CTAS CTAs;
 //   * 256 keys otherwise.
-// Measured on the 7B decode shape (32 KV heads, head_dim 128, us per call):
-// every sequence at 576 keys, 256 / 128 / 64 sequences 336 / 172 / 90 with
-// 1024-key splits against 348 / 179 / 95 with 256-key ones, 32 and 16
-// sequences 50.6 / 29.5 with 256 against 52.4 / 31.7 with two or three
-// equal splits; 8 sequences of 4096 keys 84.6 with 512 against 87.5 with 256.
+// Measured on the 7B decode shape (32 KV heads, head_dim 128, us per call,
+// 256 / 512 / 1024-key splits): every sequence at 576 keys, 256 / 128 / 64
+// sequences 348 / - / 336, 179 / - / 172, 95 / - / 89 and 32 / 16 sequences
+// 50.6 / 51.6 / 51.6, 29.5 / - / -; 8192 keys, 32 / 16 / 8 / 4 sequences
+// 604 / 594 / 589, 310 / 304 / 301, 164 / 160 / 154, 90.5 / 85.4 / 87.1;
+// 4096 keys, 32 / 8 sequences 306 / 303 / 301, 87.5 / 82.9 / 86.9.
 // LPC_DECODE_CHUNK=<keys> (a multiple of 32 from 256 to 65536) overrides the
 // choice.
 constexpr int64_t MIN_SPLIT_CTAS = 2048;
-int split_chunk(int64_t pairs, int64_t max_seq_len) {
+int split_chunk(int64_t batch, int kv_heads, int64_t total_keys) {
   static const int forced = [] {
     const char* e = getenv("LPC_DECODE_CHUNK");
     const int v = e ? atoi(e) : 0;
     return (v >= CHUNK && v <= 65536 && v % TILE == 0) ? v : 0;
   }();
   if (forced) return forced;
-  if (pairs >= MIN_SPLIT_CTAS) return 1024;
-  if (max_seq_len >= 2048 && pairs * ((max_seq_len + 511) / 512) >= MIN_SPLIT_CTAS) return 512;
+  if (batch * kv_heads >= MIN_SPLIT_CTAS) return 1024;
+  for (int c : {1024, 512})
+    if ((int64_t)kv_heads * (total_keys / c) >= MIN_SPLIT_CTAS) return c;
   return CHUNK;
 }
 
 }  // namespace
 
-extern "C" int lpc_decode_attention_split_keys(int64_t batch, int kv_heads, int64_t max_seq_len) {
+extern "C" int lpc_decode_attention_split_keys(int64_t batch, int kv_heads, int64_t max_seq_len,
+                                               int64_t total_rows) {
   if (batch <= 0 || kv_heads <= 0 || max_seq_len <= 0 || batch > MAX_DECODE_BATCH ||
-      kv_heads > MAX_DECODE_HEADS || max_seq_len > MAX_DECODE_SEQ)
+      kv_heads > MAX_DECODE_HEADS || max_seq_len > MAX_DECODE_SEQ || total_rows > (int64_t(1) << 40))
     return 0;
-  return split_chunk(batch * kv_heads, max_seq_len);
+  return split_chunk(batch, kv_heads, total_rows > 0 ? total_rows : batch * max_seq_len);
 }
 
 namespace {
@@ -650,7 +654,7 @@ int decode_common(const void* q, const void* key_cache, const void* value_cache,
   const int G = heads / kv_heads;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int ms = (int)max_splits;
-  const int ch = split_chunk(batch * kv_heads, max_seq_len);
+  const int ch = split_chunk(batch, kv_heads, rows.base ? rows.total_rows : batch * max_seq_len);
   if (dtype == LPC_DTYPE_BF16) {
     if (head_dim == 128)
       return launch_d<__nv_bfloat16, 128>(G, q, key_cache, value_cache, seq_lens, out, po, pml, batch, heads, kv_heads, max_seq_len, ms, ch, sl2, rows, s);

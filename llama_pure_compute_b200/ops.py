@@ -552,5 +552,6 @@ def decode_attention_ragged(
         workspace.numel(), B, H, Hkv, D, total_rows, max_seq_len, float(sm_scale),
         _lib.dtype_code(q.dtype, "decode_attention_ragged"), _lib.stream_of(q))
     _lib.check(rc, "decode_attention_ragged")
-    _lib.count_launch("lpc_decode_attention_ragged", _lib.decode_kernels(B, Hkv, max_seq_len))
+    _lib.count_launch("lpc_decode_attention_ragged",
+                      _lib.decode_kernels(B, Hkv, max_seq_len, total_rows))
     return out

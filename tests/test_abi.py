@@ -89,19 +89,23 @@ def test_workspace_queries():
 
 def test_decode_split_keys_rule():
     """The split length decode attention picks from its grid (host only):
-    1024 keys from 2048 (sequence, KV head) pairs up, 512 for long caches
-    whose 512-key splits still give 2048 CTAs, else 256; the launch count
-    follows (one kernel when a split covers the cache length)."""
+    1024 keys from 2048 (sequence, KV head) pairs up or when whole 1024-key
+    splits of the capacity give 2048 CTAs, 512 when whole 512-key splits do,
+    else 256; the launch count follows (one kernel when a split covers the
+    cache length)."""
     lib = _lib.load()
     sk = lib.lpc_decode_attention_split_keys
-    assert sk(256, 32, 600) == 1024 and sk(64, 32, 600) == 1024      # 8192 / 2048 pairs
-    assert sk(32, 32, 600) == 256 and sk(16, 32, 616) == 256          # 1024 / 512 pairs
-    assert sk(32, 32, 1064) == 256                                    # cache below 2048 keys
-    assert sk(8, 32, 4096) == 512 and sk(16, 32, 8192) == 512         # 256 x 8, 512 x 16 CTAs
-    assert sk(1, 32, 4096) == 256                                     # 32 x 8 < 2048
-    assert sk(0, 32, 600) == 0 and sk(4, 0, 600) == 0 and sk(4, 32, 0) == 0
-    assert _lib.decode_kernels(256, 32, 600) == 1 and _lib.decode_kernels(256, 32, 1025) == 2
-    assert _lib.decode_kernels(32, 32, 600) == 2 and _lib.decode_kernels(0, 32, 600) == 0
+    assert sk(256, 32, 616, 0) == 1024 and sk(64, 32, 616, 0) == 1024   # 8192 / 2048 pairs
+    assert sk(32, 32, 616, 0) == 256 and sk(16, 32, 616, 0) == 256     # 608 / 1216 CTAs at 1024 / 512
+    assert sk(32, 32, 1064, 0) == 512                                  # 32 x 66 whole 512-key splits
+    assert sk(8, 32, 4096, 0) == 512 and sk(4, 32, 8232, 0) == 512     # 32 x 64 whole 512-key splits
+    assert sk(8, 32, 8232, 0) == 1024 and sk(16, 32, 8192, 0) == 1024  # 32 x 64 / 128 whole 1024
+    assert sk(1, 32, 4096, 0) == 256
+    # ragged: the rows per KV head stand for the capacity, not batch * max_seq_len
+    assert sk(8, 32, 8448, 39000) == 512 and sk(8, 32, 8448, 66000) == 1024
+    assert sk(0, 32, 600, 0) == 0 and sk(4, 0, 600, 0) == 0 and sk(4, 32, 0, 0) == 0
+    assert _lib.decode_kernels(256, 32, 616) == 1 and _lib.decode_kernels(256, 32, 1025) == 2
+    assert _lib.decode_kernels(32, 32, 616) == 2 and _lib.decode_kernels(0, 32, 616) == 0
 
 
 def test_read_probe_validates_on_the_host():
