@@ -578,6 +578,17 @@ def test_decode_independent_of_workspace_contents(H, Hkv):
     assert o1[1].abs().sum().item() == 0
 
 
+def test_hbm_read_probe_runs_clean():
+    """The read-rate probe the bench reports beside the copy peak: reads a
+    256 MB buffer, returns 0 and leaves the device status clean."""
+    buf = torch.zeros(256 << 20, dtype=torch.uint8, device=DEV)
+    lib = _lib.load()
+    st = torch.cuda.current_stream().cuda_stream
+    assert lib.lpc_hbm_read_probe(buf.data_ptr(), buf.numel(), st) == 0
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+
+
 @pytest.mark.parametrize("B,Smax,lens", [
     # 64 x 32 (sequence, KV head) pairs, a cache of <= 1024 keys: one split
     # of up to 1024 keys per sequence, no combine launch

@@ -89,6 +89,34 @@ def test_decode_attention_ragged_matches_dense_and_oracle(G):
     assert (o_rag.float().cpu() - ref).abs().max().item() < 2e-2
 
 
+def test_decode_attention_ragged_one_split_matches_dense():
+    """64 sequences x 32 KV heads: both layouts take one 1024-key split per
+    sequence and KV head and launch no combine kernel; outputs bit-identical,
+    an empty context gives zeros."""
+    g = torch.Generator(device=DEV).manual_seed(11)
+    D, Hkv, B = 128, 32, 64
+    caps = [1000 - 7 * (b % 9) for b in range(B)]
+    lens = [c - (b % 5) * 100 for b, c in enumerate(caps)]
+    lens[3] = 0
+    Smax = max(caps)
+    seq_base, seq_cap, total, base = ragged_index(caps)
+    assert _lib.decode_kernels(B, Hkv, Smax) == 1 and _lib.decode_kernels(B, Hkv, Smax, total) == 1
+    kd = torch.randn(B, Hkv, Smax, D, device=DEV, generator=g).to(torch.bfloat16)
+    vd = torch.randn(B, Hkv, Smax, D, device=DEV, generator=g).to(torch.bfloat16)
+    kr = dense_to_ragged(kd, caps, base, total)
+    vr = dense_to_ragged(vd, caps, base, total)
+    q = torch.randn(B, Hkv, D, device=DEV, generator=g).to(torch.bfloat16)
+    L = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    o_dense = ops.decode_attention(q, kd, vd, L)
+    o_rag = ops.decode_attention_ragged(q, kr, vr, L, seq_base, seq_cap, Smax)
+    assert torch.equal(o_dense, o_rag)
+    assert o_rag[3].abs().sum().item() == 0
+    sel = [0, 3, 17, 63]
+    ref = decode_attention_ref(q[sel].float().cpu(), kd[sel].float().cpu(), vd[sel].float().cpu(),
+                               L[sel].cpu())
+    assert (o_rag[sel].float().cpu() - ref).abs().max().item() < 2e-2
+
+
 def test_ragged_out_of_range_rows_are_flagged_not_read():
     D, Hkv, H = 128, 2, 2
     caps = [64, 64]
