@@ -108,6 +108,22 @@ def test_decode_split_keys_rule():
     assert _lib.decode_kernels(32, 32, 616) == 2 and _lib.decode_kernels(0, 32, 616) == 0
 
 
+def test_decode_split_keys_override():
+    """LPC_DECODE_CHUNK forces the split length (read once per process, so
+    each case runs in a fresh interpreter); values that are not a multiple of
+    32 in [256, 65536] are ignored."""
+    import os
+    import sys
+    code = ("from llama_pure_compute_b200 import _lib; "
+            "print(_lib.load().lpc_decode_attention_split_keys(256, 32, 616, 0))")
+    for forced, want in (("512", 512), ("2048", 2048), ("300", 1024), ("128", 1024)):
+        env = dict(os.environ, LPC_DECODE_CHUNK=forced)
+        out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                             cwd=Path(__file__).resolve().parents[1], timeout=120)
+        assert out.returncode == 0, out.stderr[-500:]
+        assert int(out.stdout.strip().splitlines()[-1]) == want, forced
+
+
 def test_read_probe_validates_on_the_host():
     lib = _lib.load()
     assert lib.lpc_hbm_read_probe(None, 131072, None) == _lib.LPC_ERR_INVALID
