@@ -15,6 +15,8 @@
 // loads the VEC lower-half and VEC upper-half elements as 16-byte vectors.
 #include <algorithm>
 
+#include <cstdlib>
+
 #include "lpc_common.cuh"
 
 LPC_DECLARE_STATUS(g_rope_status)
@@ -171,6 +173,11 @@ __global__ void __launch_bounds__(RA_THREADS, 3) rope_kv_append_kernel(
     T* __restrict__ kcache, T* __restrict__ vcache, int64_t seq, int num_heads, int num_kv_heads,
     int head_dim, int chunks, int hpb, int64_t max_batch, int64_t max_seq_len,
     const int64_t* __restrict__ seq_base, const int32_t* __restrict__ seq_cap, int64_t total_rows) {
+  // launched with programmatic stream serialisation: the decode attention
+  // after it may be scheduled now (it waits for this grid before reading the
+  // cache), and this grid waits for the projection that wrote qkv
+  lpc::pdl_trigger();
+  lpc::pdl_wait();
   const int half = head_dim >> 1;
   const int heads_all = num_heads + 2 * num_kv_heads;
   const int64_t tok = blockIdx.x;  // b * seq + s
@@ -286,15 +293,29 @@ int launch_rope_t(int table_dtype, void* q, void* k, const void* c, const void* 
 }
 
 template <typename T, typename TT, int K>
-void launch_fused_k(dim3 grid, int threads, const void* qkv, const int64_t* positions,
+cudaError_t launch_fused_k(dim3 grid, int threads, const void* qkv, const int64_t* positions,
                     const void* c, const void* sn, int64_t rows, void* q_out, void* kc, void* vc,
                     int64_t seq, int h, int hkv, int d, int chunks, int hpb, int64_t max_batch,
                     int64_t max_seq, const int64_t* seq_base, const int32_t* seq_cap,
                     int64_t total_rows, cudaStream_t s) {
   constexpr int VEC = 16 / (int)sizeof(T);
-  rope_kv_append_kernel<T, TT, VEC, K><<<grid, threads, 0, s>>>(
-      (const T*)qkv, positions, (const TT*)c, (const TT*)sn, rows, (T*)q_out, (T*)kc, (T*)vc, seq,
-      h, hkv, d, chunks, hpb, max_batch, max_seq, seq_base, seq_cap, total_rows);
+  static const bool pdl = [] {
+    const char* e = getenv("LPC_PDL");
+    return !(e && e[0] == '0');
+  }();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3((unsigned)threads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, rope_kv_append_kernel<T, TT, VEC, K>, (const T*)qkv, positions,
+                     (const TT*)c, (const TT*)sn, rows, (T*)q_out, (T*)kc, (T*)vc, seq, h, hkv, d,
+                     chunks, hpb, max_batch, max_seq, seq_base, seq_cap, total_rows);
 }
 
 template <typename T, typename TT>
@@ -319,14 +340,11 @@ int launch_fused(const void* qkv, const int64_t* positions, const void* c, const
 #define LPC_RA(KK)                                                                                 \
   launch_fused_k<T, TT, KK>(grid, threads, qkv, positions, c, sn, rows, q_out, kc, vc, seq, h, hkv, \
                             d, chunks, hpb, max_batch, max_seq, seq_base, seq_cap, total_rows, s)
-  if (K == 1)
-    LPC_RA(1);
-  else if (K == 2)
-    LPC_RA(2);
-  else if (K == 3)
-    LPC_RA(3);
-  else
-    LPC_RA(4);
+  const cudaError_t e = K == 1 ? LPC_RA(1) : K == 2 ? LPC_RA(2) : K == 3 ? LPC_RA(3) : LPC_RA(4);
+  if (e != cudaSuccess) {
+    lpc::set_error("rope_kv_append: launch failed: %s", cudaGetErrorString(e));
+    return LPC_ERR_CUDA;
+  }
 #undef LPC_RA
   return lpc::check_launch("rope_kv_append");
 }
